@@ -1,0 +1,118 @@
+/*
+ * vibegemm_b200.h — C ABI of the B200 (sm_100a) FP16 GEMM backend.
+ *
+ * Semantics of every GEMM entry point (identical to the reference backends):
+ *   C[m*N + n] = fp16_rn( sum_k float(A[m*K + k]) * float(B[n*K + k]) )
+ *   A: M×K fp16 row-major; B: N×K fp16 (K contiguous, i.e. "K×N column-major");
+ *   C: M×N row-major; alpha = 1, beta = 0; C is fully overwritten; fp32 accumulate.
+ *   All pointers are device pointers owned by the caller.
+ *
+ * Return values are cudaError_t codes (0 = cudaSuccess). Launches are asynchronous
+ * on `stream` (NULL = the legacy default stream, which is where the reference
+ * engine records its timing events). Asynchronous device faults surface at the
+ * caller's next synchronisation, as with the reference's cuda_check().
+ *
+ * Plain C types only: pointers, ints and an opaque stream handle that is
+ * ABI-identical to cudaStream_t.
+ */
+#ifndef VIBEGEMM_B200_H
+#define VIBEGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *vg_stream_t;
+
+/* Default B200 kernel (the fastest registered version).
+ * Replaces GemmBackend::run (include/backend.cuh:13) of a registered backend and the
+ * per-version free function launchKernel(half*,half*,half*,int,int,int)
+ * (csrc/h100/gemm_8192x8192_v18.cuh:545, bound through csrc/gemm_h100_backends.cu:41). */
+int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
+                     vg_stream_t stream);
+
+/* One specific kernel version of the B200 ladder, 0 <= version < vg_b200_num_versions().
+ * Replaces gemm_8192x8192_vN::launchKernel (csrc/h100/gemm_8192x8192_v*.cuh), one per
+ * registered "VibeGEMM B200 vN" backend (registry.cuh:68-70 pattern). */
+int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C, int M, int N,
+                             int K, vg_stream_t stream);
+
+/* Validation build: the same main loop as `version`, fp32 C (no fp16 rounding), so
+ * accumulation error can be judged separately from output quantisation. No
+ * counterpart in the reference (its only check is fp16-vs-cuBLAS,
+ * include/utils.cuh:70-118). */
+int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C, int M, int N,
+                            int K, vg_stream_t stream);
+
+/* cuBLAS yardstick with the row-major-C operand order.
+ * Replaces CublasBackend::run (csrc/cublas_backends.cu:21-35, the HAS_A100 branch
+ * :28-31, which writes row-major C) — the reference judge. */
+int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
+                       vg_stream_t stream);
+
+/* Registry listing: replaces KernelRegistry::make_all / GemmBackend::name
+ * (include/registry.cuh:23-32, include/backend.cuh:16). */
+int vg_b200_num_versions(void);
+const char *vg_b200_version_name(int version);
+int vg_b200_default_version(void);
+
+/* Replaces GemmBackend::is_available (include/backend.cuh:24): 1 if `device` is an
+ * sm_100 part this library was built for, 0 otherwise (never throws). */
+int vg_b200_is_available(int device);
+
+/* Replaces GemmBackend::teardown (include/backend.cuh:20): drops cached tensor maps
+ * and launch configuration of the calling thread. */
+void vg_b200_teardown(void);
+
+/* Failure detection (no reference counterpart; the reference only has the
+ * non-fatal CUDA_TRY / cuda_check, include/utils.cuh:13-30). Every device wait in the
+ * kernels is bounded by the timeout below; a wait that runs out records a nonzero
+ * status word on the device and the kernel unwinds instead of hanging. */
+unsigned vg_b200_device_status(int reset); /* synchronous read of the status word */
+int vg_b200_set_wait_timeout_ns(unsigned long long ns); /* 0 restores the default (2 s) */
+/* Launches a kernel that waits on a barrier nothing arrives on, bounded by
+ * `timeout_ns`; returns 1 if the wait correctly gave up and recorded its status. */
+int vg_b200_selftest_wait_timeout(unsigned long long timeout_ns);
+
+/* Contiguous row-block sharding used by the multi-GPU driver (A and C split by rows,
+ * B replicated): rank r of `world` owns rows [row0, row0 + rows). No reference
+ * counterpart (the reference is single-device, main.cu:70). */
+void vg_shard_rows(long long M, int world, int rank, long long *row0, long long *rows);
+
+/* Grouped-raster tile order used by the persistent kernels: linear tile index t ->
+ * (tile_m, tile_n). Replaces Schedule::next (csrc/h100/gemm_8192x8192_v18.cuh:207-260). */
+void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *tile_n);
+
+/* Host-side launch plan for a problem, as the launcher would build it for a device
+ * with `num_sms` SMs (exposed so the planner can be tested without a GPU).
+ * Fields of `out` (int[12]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct
+ * fp16, 2 direct fp32), pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb,
+ * group_m, grid (CTAs), persistent. Returns 0 or a cudaError_t code for bad input. */
+int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
+                 int f32_out, int num_sms, int *out);
+
+/* Reference-facing plugin path: runs registered backend `name` (e.g. "cuBLAS",
+ * "VibeGEMM B200 v2") through GemmBackend::run on the legacy default stream.
+ * Returns cudaErrorInvalidValue if no backend has that name. */
+int vg_backend_count(void);
+const char *vg_backend_name(int i);
+int vg_backend_run(const char *name, void *A, void *B, void *C, int M, int N, int K);
+
+/* The reference engine (include/engine.cuh) run over every registered backend for
+ * one shape: reference = cuBLAS, 10 warm-up + 30 timed launches, then the
+ * element-wise check (replaces BenchmarkEngine::execute, include/engine.cuh:20-86).
+ * `inputs`: 0 = uniform[-1,1] (seeds 42/77, the reference's), 1 = N(0, 0.02).
+ * `log_path` may be NULL. Results of the last call are readable per backend. */
+int vg_engine_execute(int M, int N, int K, int inputs, const char *log_path);
+int vg_engine_result_count(void);
+/* out: [avg_ms, tflops, max_abs_err, max_rel_err, passed(0/1), skipped(0/1)] */
+int vg_engine_result(int i, char *name_buf, int name_len, double *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VIBEGEMM_B200_H */

@@ -1,0 +1,107 @@
+"""C ABI: the library loads without a GPU, exports every declared symbol, and its host
+logic (planner, raster order, row sharding, registry) behaves. No compute calls."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(vg_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol(vg):
+    decl = declared_symbols()
+    assert len(decl) >= 20
+    L = ctypes.CDLL(str(vg.LIB_PATH))
+    missing = [n for n in decl if not hasattr(L, n)]
+    assert not missing, missing
+    assert set(decl) == set(vg.EXPORTED_SYMBOLS)
+
+
+def test_versions_and_registry_order(vg):
+    assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2"]
+    assert vg.default_version() == 2
+    # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
+    assert vg.backends() == ["cuBLAS"] + vg.versions()
+
+
+@pytest.mark.parametrize("num_m,num_n,group", [(1, 1, 8), (32, 32, 8), (7, 13, 8), (33, 5, 4),
+                                               (100, 3, 16), (5, 41, 1), (9, 9, 100)])
+def test_raster_is_a_bijection(vg, num_m, num_n, group):
+    seen = set()
+    for t in range(num_m * num_n):
+        tm, tn = vg.raster_tile(t, num_m, num_n, group)
+        assert 0 <= tm < num_m and 0 <= tn < num_n
+        seen.add((tm, tn))
+    assert len(seen) == num_m * num_n
+    assert vg.raster_tile(num_m * num_n, num_m, num_n, group) == (-1, -1)
+
+
+def test_raster_groups_m_tiles(vg):
+    # Consecutive tiles walk down a group of 8 M tiles before moving along N.
+    order = [vg.raster_tile(t, 32, 32, 8) for t in range(16)]
+    assert order[:8] == [(m, 0) for m in range(8)]
+    assert order[8:16] == [(m, 1) for m in range(8)]
+
+
+@pytest.mark.parametrize("M,world", [(32768, 1), (32768, 2), (32768, 8), (8191, 8), (3, 8), (0, 4)])
+def test_shard_rows_partition(vg, M, world):
+    covered = []
+    for r in range(world):
+        r0, n = vg.shard_rows(M, world, r)
+        assert n >= 0
+        covered.extend(range(r0, r0 + n))
+    assert covered == list(range(M))
+
+
+def test_plan_aligned_square(vg):
+    p = vg.plan(2, 8192, 8192, 8192, 256, 256, 256)
+    assert p["cta_group"] == 2 and p["epilogue"] == "tma_f16"
+    assert (p["pad_a"], p["pad_b"]) == (0, 0)
+    assert (p["num_m_tiles"], p["num_n_tiles"], p["num_kb"]) == (32, 32, 128)
+    assert p["grid"] == 148 and p["persistent"] == 1
+    p1 = vg.plan(1, 8192, 8192, 8192, 256, 256, 256)
+    assert p1["cta_group"] == 1 and p1["grid"] == 148 and p1["num_m_tiles"] == 64
+    p0 = vg.plan(0, 8192, 8192, 8192, 256, 256, 256)
+    assert p0["persistent"] == 0 and p0["grid"] == 64 * 32 and p0["epilogue"] == "direct_f16"
+
+
+def test_plan_tails_and_alignment(vg):
+    # 8191x8193x4099: K*2 bytes not a multiple of 16 -> both operands padded to K=4104;
+    # N*2 not a multiple of 16 -> direct-store epilogue.
+    p = vg.plan(2, 8191, 8193, 4099, 256, 256, 256)
+    assert (p["pad_a"], p["pad_b"], p["k_padded"]) == (1, 1, 4104)
+    assert p["epilogue"] == "direct_f16"
+    assert (p["num_m_tiles"], p["num_n_tiles"], p["num_kb"]) == (32, 33, 65)
+    # 1000x3000x2048: aligned strides, partial tiles, under-filled grid.
+    p = vg.plan(2, 1000, 3000, 2048, 256, 256, 256)
+    assert (p["pad_a"], p["pad_b"], p["epilogue"]) == (0, 0, "tma_f16")
+    assert p["grid"] == 2 * 4 * 12
+    # A misaligned pointer alone pads only that operand.
+    p = vg.plan(2, 512, 512, 512, 258, 256, 256)
+    assert (p["pad_a"], p["pad_b"]) == (1, 0)
+    # A misaligned C pointer switches to direct stores; fp32 output always direct.
+    assert vg.plan(2, 512, 512, 512, 256, 256, 258)["epilogue"] == "direct_f16"
+    assert vg.plan(2, 512, 512, 512, 256, 256, 256, f32_out=True)["epilogue"] == "direct_f32"
+
+
+def test_plan_rejects_bad_input(vg):
+    with pytest.raises(vg.VibeGemmError):
+        vg.plan(7, 16, 16, 16)
+    with pytest.raises(vg.VibeGemmError):
+        vg.plan(0, -1, 16, 16)
+
+
+def test_gemm_rejects_cpu_tensors(vg):
+    import torch
+    a = torch.zeros(4, 8, dtype=torch.float16)
+    with pytest.raises(ValueError):
+        vg.gemm(a, a)

@@ -1,0 +1,157 @@
+"""Parity of every B200 kernel version with the oracle (CPU restatement of the reference
+GEMM) and with the reference's judge (cuBLAS), through the C ABI.
+
+Bars (written here, per the reference's validation):
+  * fp16 output: the reference's check_error (|r-c| <= 1e-3 + 1e-2*|r|, include/utils.cuh:70-118)
+    against the oracle's fp16 result and against cuBLAS, plus at most 1 fp16 ulp of difference
+    from the oracle wherever |C| >= 2^-4 (fp32 accumulation-order noise can flip one rounding);
+  * fp32 validation output: max abs error <= 2e-2*sqrt(K/1024) and max relative error
+    |c-r|/max(|r|, that bound) <= 1e-2 against the fp64-accumulated product.
+"""
+import numpy as np
+import pytest
+
+from conftest import to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+VERSIONS = [0, 1, 2]
+# (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
+# epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
+SHAPES = [
+    (512, 512, 512, "uniform"),
+    (320, 512, 200, "uniform"),
+    (257, 263, 72, "uniform"),
+    (1, 1, 8, "uniform"),
+    (1, 256, 64, "uniform"),
+    (128, 256, 64, "uniform"),
+    (130, 70, 24, "uniform"),
+    (129, 257, 65, "uniform"),
+    (300, 1001, 136, "uniform"),
+    (200, 520, 4099, "uniform"),
+    (256, 1024, 512, "normal"),
+    (1000, 3000, 2048, "uniform"),
+]
+
+
+def ulp_diff(a_bits, b_bits):
+    def key(x):
+        x = x.astype(np.int32)
+        return np.where(x & 0x8000, -(x & 0x7FFF), x & 0x7FFF)
+    return np.abs(key(a_bits) - key(b_bits))
+
+
+def check_fp16(orc, got, ref, what):
+    ok, st = orc.check_error(ref, got)
+    assert ok, (what, st)
+    big = np.abs(ref.view(np.float16).astype(np.float32)) >= 2.0 ** -4
+    if big.any():
+        assert ulp_diff(got[big], ref[big]).max() <= 1, what
+
+
+@pytest.fixture(scope="module")
+def cases(orc):
+    out = {}
+    for (M, N, K, dist) in SHAPES:
+        A, B = orc.make_inputs(M, N, K, dist)
+        out[(M, N, K, dist)] = (A, B, orc.gemm_f16(A, B), orc.gemm_f64(A, B))
+    return out
+
+
+@pytest.mark.parametrize("version", VERSIONS)
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s[:3])) + "_" + s[3])
+def test_fp16_matches_oracle_and_cublas(vg, orc, cases, version, shape):
+    import torch
+    A, B, ref16, _ = cases[shape]
+    dA, dB = to_dev(A), to_dev(B)
+    C = vg.gemm(dA, dB, version=version)
+    Cb = vg.cublas_gemm(dA, dB)
+    torch.cuda.synchronize()
+    got, cub = to_host(C), to_host(Cb)
+    check_fp16(orc, got, ref16, f"v{version} vs oracle {shape}")
+    ok, st = orc.check_error(cub, got)
+    assert ok, ("vs cuBLAS", st)
+    assert vg.device_status() == 0
+
+
+@pytest.mark.parametrize("version", VERSIONS)
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s[:3])) + "_" + s[3])
+def test_fp32_accumulation_within_bounds(vg, orc, cases, version, shape):
+    import torch
+    A, B, _, exact = cases[shape]
+    C = vg.gemm_f32out(to_dev(A), to_dev(B), version=version)
+    torch.cuda.synchronize()
+    acc = orc.acceptance(C.cpu().numpy(), exact, K=shape[2])
+    assert acc["max_abs"] <= acc["abs_bound"], acc
+    assert acc["max_rel"] <= 1e-2, acc
+
+
+@pytest.mark.parametrize("version", VERSIONS)
+def test_misaligned_operands(vg, orc, version):
+    """Pointers off the 16-B grid: A and B go through the pad pre-pass, C through direct stores."""
+    import torch
+    M, N, K = 190, 300, 96
+    A, B = orc.make_inputs(M, N, K)
+    ref = orc.gemm_f16(A, B)
+    bufA = torch.zeros(M * K + 8, dtype=torch.float16, device="cuda")
+    bufB = torch.zeros(N * K + 8, dtype=torch.float16, device="cuda")
+    bufC = torch.zeros(M * N + 8, dtype=torch.float16, device="cuda")
+    dA = bufA[1:1 + M * K].view(M, K)
+    dB = bufB[3:3 + N * K].view(N, K)
+    dA.copy_(to_dev(A))
+    dB.copy_(to_dev(B))
+    C = bufC[5:5 + M * N].view(M, N)
+    vg.gemm(dA, dB, out=C, version=version)
+    torch.cuda.synchronize()
+    check_fp16(orc, to_host(C), ref, "misaligned")
+    # The guard elements around C are untouched.
+    assert float(bufC[:5].abs().sum()) == 0.0 and float(bufC[5 + M * N:].abs().sum()) == 0.0
+
+
+@pytest.mark.parametrize("version", VERSIONS)
+def test_degenerate_sizes(vg, version):
+    import torch
+    A = torch.randn(64, 0, device="cuda").half()
+    B = torch.randn(32, 0, device="cuda").half()
+    C = torch.full((64, 32), 7.0, device="cuda").half()
+    vg.gemm(A, B, out=C, version=version)           # K = 0 -> C = 0
+    torch.cuda.synchronize()
+    assert float(C.abs().sum()) == 0.0
+    E = vg.gemm(torch.zeros(0, 16, device="cuda").half(), torch.zeros(8, 16, device="cuda").half())
+    assert E.shape == (0, 8)
+
+
+def test_output_fully_overwritten_and_inputs_untouched(vg, orc):
+    import torch
+    M, N, K = 384, 768, 256
+    A, B = orc.make_inputs(M, N, K)
+    dA, dB = to_dev(A), to_dev(B)
+    C = torch.full((M, N), float("nan"), device="cuda").half()
+    vg.gemm(dA, dB, out=C)
+    torch.cuda.synchronize()
+    assert not torch.isnan(C).any()
+    assert np.array_equal(to_host(dA), A) and np.array_equal(to_host(dB), B)
+
+
+def test_stream_argument(vg, orc):
+    import torch
+    M, N, K = 256, 512, 128
+    A, B = orc.make_inputs(M, N, K)
+    s = torch.cuda.Stream()
+    dA, dB = to_dev(A), to_dev(B)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        C = vg.gemm(dA, dB, stream=s)
+    s.synchronize()
+    check_fp16(orc, to_host(C), orc.gemm_f16(A, B), "stream")
+
+
+def test_repeated_calls_deterministic(vg, orc):
+    import torch
+    A, B = orc.make_inputs(640, 1280, 384)
+    dA, dB = to_dev(A), to_dev(B)
+    first = vg.gemm(dA, dB).clone()
+    for _ in range(5):
+        again = vg.gemm(dA, dB)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)

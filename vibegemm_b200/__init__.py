@@ -1,0 +1,228 @@
+"""VibeGEMM-B200: FP16 GEMM (fp32 accumulate, fp16 out) for NVIDIA B200 (sm_100a).
+
+Python bindings over the C ABI in ``include/vibegemm_b200.h`` (``libvibegemm_b200.so``,
+built in-tree by :mod:`vibegemm_b200.build`). Device buffers are torch tensors; the
+kernels themselves are the hand-written tcgen05/TMA kernels of the library. There is no
+fallback: if the library is missing, :func:`lib` raises, and every GEMM entry point
+requires CUDA tensors.
+
+Layout convention (the reference's): ``A`` is M×K row-major, ``B`` is stored N×K
+(K contiguous), ``C = A @ B.T`` is M×N row-major.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libvibegemm_b200.so"
+_lib: Optional[ctypes.CDLL] = None
+
+# Names exported by the C ABI (include/vibegemm_b200.h), with their signatures.
+_SIGS = {
+    "vg_b200_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_b200_gemm_f16_version": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_b200_gemm_f16_f32out": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_cublas_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_b200_num_versions": (ctypes.c_int, []),
+    "vg_b200_version_name": (ctypes.c_char_p, [ctypes.c_int]),
+    "vg_b200_default_version": (ctypes.c_int, []),
+    "vg_b200_is_available": (ctypes.c_int, [ctypes.c_int]),
+    "vg_b200_teardown": (None, []),
+    "vg_b200_device_status": (ctypes.c_uint, [ctypes.c_int]),
+    "vg_b200_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_ulonglong]),
+    "vg_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_ulonglong]),
+    "vg_shard_rows": (None, [ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
+                             ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong)]),
+    "vg_raster_tile": (None, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2),
+    "vg_b200_plan": (ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.c_size_t] * 3 + [ctypes.c_int] * 2
+                     + [ctypes.POINTER(ctypes.c_int)]),
+    "vg_backend_count": (ctypes.c_int, []),
+    "vg_backend_name": (ctypes.c_char_p, [ctypes.c_int]),
+    "vg_backend_run": (ctypes.c_int, [ctypes.c_char_p] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3),
+    "vg_engine_execute": (ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.c_char_p]),
+    "vg_engine_result_count": (ctypes.c_int, []),
+    "vg_engine_result": (ctypes.c_int, [ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_double)]),
+}
+EXPORTED_SYMBOLS = tuple(_SIGS)
+
+PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
+               "num_n_tiles", "num_kb", "group_m", "grid", "persistent")
+EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32"}
+
+
+class VibeGemmError(RuntimeError):
+    """A C-ABI call returned a nonzero status (a cudaError_t code, or 1000 + cuBLAS status)."""
+
+    def __init__(self, what: str, code: int):
+        super().__init__(f"{what} failed with status {code}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C library. Raises ImportError when it has not been built."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("VIBEGEMM_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise ImportError(f"{path} is missing: build it with `python -m vibegemm_b200.build` "
+                              "(there is no fallback implementation)")
+        handle = ctypes.CDLL(str(path), mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def _check(code: int, what: str) -> None:
+    if code != 0:
+        raise VibeGemmError(what, code)
+
+
+def _stream_handle(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream or None
+    if isinstance(stream, int):
+        return stream or None
+    return stream.cuda_stream or None
+
+
+def _operands(A, B, out, out_dtype):
+    import torch
+    if not (A.is_cuda and B.is_cuda):
+        raise ValueError("A and B must be CUDA tensors (no CPU path)")
+    if A.dtype != torch.float16 or B.dtype != torch.float16:
+        raise TypeError("A and B must be float16")
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[1]:
+        raise ValueError(f"expected A[M,K] and B[N,K], got {tuple(A.shape)} and {tuple(B.shape)}")
+    if not (A.is_contiguous() and B.is_contiguous()):
+        raise ValueError("A and B must be contiguous (row-major)")
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    elif out.shape != (M, N) or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [M, N] tensor of the output dtype")
+    return int(M), int(N), int(K), out
+
+
+def gemm(A, B, out=None, version: Optional[int] = None, stream=None):
+    """C = A @ B.T on the B200 kernel (`version` of the ladder, default = fastest)."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float16)
+    s = _stream_handle(stream)
+    if version is None:
+        code = lib().vg_b200_gemm_f16(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K, s)
+    else:
+        code = lib().vg_b200_gemm_f16_version(version, A.data_ptr(), B.data_ptr(), out.data_ptr(),
+                                              M, N, K, s)
+    _check(code, "vg_b200_gemm_f16")
+    return out
+
+
+def gemm_f32out(A, B, out=None, version: Optional[int] = None, stream=None):
+    """Validation build: same main loop, fp32 C (no output rounding)."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float32)
+    v = default_version() if version is None else version
+    code = lib().vg_b200_gemm_f16_f32out(v, A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K,
+                                         _stream_handle(stream))
+    _check(code, "vg_b200_gemm_f16_f32out")
+    return out
+
+
+def cublas_gemm(A, B, out=None, stream=None):
+    """The cuBLAS yardstick (cublasGemmEx, COMPUTE_32F, row-major C)."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float16)
+    code = lib().vg_cublas_gemm_f16(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K,
+                                    _stream_handle(stream))
+    _check(code, "vg_cublas_gemm_f16")
+    return out
+
+
+def versions() -> list[str]:
+    L = lib()
+    return [L.vg_b200_version_name(i).decode() for i in range(L.vg_b200_num_versions())]
+
+
+def default_version() -> int:
+    return int(lib().vg_b200_default_version())
+
+
+def is_available(device: int = 0) -> bool:
+    return bool(lib().vg_b200_is_available(device))
+
+
+def teardown() -> None:
+    lib().vg_b200_teardown()
+
+
+def device_status(reset: bool = False) -> int:
+    return int(lib().vg_b200_device_status(1 if reset else 0))
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    lib().vg_b200_set_wait_timeout_ns(ns)
+
+
+def selftest_wait_timeout(timeout_ns: int) -> bool:
+    return bool(lib().vg_b200_selftest_wait_timeout(timeout_ns))
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    r0, n = ctypes.c_longlong(), ctypes.c_longlong()
+    lib().vg_shard_rows(M, world, rank, ctypes.byref(r0), ctypes.byref(n))
+    return int(r0.value), int(n.value)
+
+
+def raster_tile(t: int, num_m: int, num_n: int, group_m: int) -> tuple[int, int]:
+    tm, tn = ctypes.c_int(), ctypes.c_int()
+    lib().vg_raster_tile(t, num_m, num_n, group_m, ctypes.byref(tm), ctypes.byref(tn))
+    return int(tm.value), int(tn.value)
+
+
+def plan(version: int, M: int, N: int, K: int, a_ptr: int = 0, b_ptr: int = 0, c_ptr: int = 0,
+         f32_out: bool = False, num_sms: int = 148) -> dict:
+    out = (ctypes.c_int * 12)()
+    _check(lib().vg_b200_plan(version, M, N, K, a_ptr, b_ptr, c_ptr, int(f32_out), num_sms, out),
+           "vg_b200_plan")
+    d = dict(zip(PLAN_FIELDS, list(out)))
+    d["epilogue"] = EPILOGUES[d["epilogue"]]
+    return d
+
+
+def backends() -> list[str]:
+    L = lib()
+    return [L.vg_backend_name(i).decode() for i in range(L.vg_backend_count())]
+
+
+def backend_run(name: str, A, B, C) -> None:
+    """Run registered backend `name` through GemmBackend::run (legacy default stream)."""
+    M, K = A.shape
+    N = B.shape[0]
+    _check(lib().vg_backend_run(name.encode(), A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K),
+           f"backend {name!r}")
+
+
+def engine_execute(M: int, N: int, K: int, inputs: str = "uniform",
+                   log_path: Optional[str] = None) -> list[dict]:
+    """BenchmarkEngine::execute over every registered backend; returns per-backend results."""
+    L = lib()
+    _check(L.vg_engine_execute(M, N, K, 1 if inputs == "normal" else 0,
+                               log_path.encode() if log_path else None), "vg_engine_execute")
+    res = []
+    buf = ctypes.create_string_buffer(256)
+    vals = (ctypes.c_double * 6)()
+    for i in range(L.vg_engine_result_count()):
+        _check(L.vg_engine_result(i, buf, 256, vals), "vg_engine_result")
+        res.append({"name": buf.value.decode(), "avg_ms": vals[0], "tflops": vals[1],
+                    "max_abs_err": vals[2], "max_rel_err": vals[3], "passed": bool(vals[4]),
+                    "skipped": bool(vals[5])})
+    return res

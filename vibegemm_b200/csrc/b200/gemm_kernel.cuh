@@ -1,0 +1,477 @@
+// FP16 GEMM on sm_100a tensor cores: C[M,N] = A[M,K] · B[N,K]^T, fp32 accumulate.
+//
+// Semantics follow the reference layout convention (A row-major M×K, B stored N×K
+// with K contiguous, C row-major M×N; csrc/a100/gemm_8192x8192_v0.cuh:45,54,72 and
+// the naive kernel csrc/h100/gemm_8192x8192_v8.cuh:347-358). Design is B200-native:
+//
+//   warp 0      TMA producer: A and B k-blocks (64 fp16 = one 128-B swizzle row)
+//               into a STAGES-deep shared-memory ring guarded by full/empty mbarriers.
+//   warp 1      TMEM owner (alloc 512 columns = two 128×256 fp32 accumulators) and,
+//               in the leader CTA, the single-thread tcgen05.mma issuer.
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes × 32 columns) → cvt.rn fp16 →
+//               either 128-B-swizzled smem staging + TMA store (aligned C) or
+//               predicated direct stores (unaligned C / fp32 validation output).
+//
+// CG = 1: one CTA computes a 128×256 tile with tcgen05.mma.cta_group::1 (M=128,N=256).
+// CG = 2: a CTA pair computes a 256×256 tile with tcgen05.mma.cta_group::2 (M=256,
+//         N=256). Each CTA loads its own 128 rows of A and its own 128 rows of B with
+//         ordinary (non-multicast) TMA loads whose completion is counted on the
+//         leader's barrier; the leader issues the MMAs, and tcgen05.commit arrives on
+//         both CTAs' barriers. Each CTA's TMEM holds its 128 rows of the tile.
+//
+// The accumulator is double-buffered in TMEM, so the epilogue of tile i overlaps the
+// main loop of tile i+1. Tiles are visited persistently with a grouped raster.
+//
+// Every mbarrier wait is bounded: after `timeout_ns` without progress the waiting
+// thread records a code in `vg_status_word`, raises a CTA-local abort flag and all
+// roles unwind to the common exit, which still drains outstanding copies and frees
+// TMEM. A healthy wait lasts microseconds.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "schedule.cuh"
+
+namespace vg {
+
+enum EpiKind : int {
+    kEpiTmaF16 = 0,    // smem staging + TMA store (C 16-B aligned, ldc % 8 == 0)
+    kEpiDirectF16 = 1, // predicated global stores (any C alignment / ldc)
+    kEpiDirectF32 = 2, // fp32 output, validation build of the same main loop
+};
+
+// Status codes written to vg_status_word (first writer wins).
+enum StatusCode : unsigned {
+    kStatusOk = 0,
+    kStatusTimeoutProducer = 0x101,
+    kStatusTimeoutMma = 0x102,
+    kStatusTimeoutEpilogue = 0x103,
+    kStatusTimeoutDrain = 0x104,
+    kStatusTimeoutSelftest = 0x1FF,
+};
+
+struct GemmArgs {
+    int M, N, K;
+    int num_m_tiles; // tiles of 128*CG rows
+    int num_n_tiles; // tiles of 256 columns
+    int num_kb;      // ceil(K / 64)
+    int group_m;     // raster group height (in M tiles)
+    int c_vec_ok;    // direct epilogue may use 16-B stores
+    void *C;         // direct epilogues only
+    long long ldc;   // elements
+    unsigned long long timeout_ns;
+};
+
+template <int CG> struct TileCfg {
+    static constexpr int BM = 128;          // accumulator rows per CTA (TMEM lanes)
+    static constexpr int BN = 256;          // tile columns (fp32 TMEM columns per buffer)
+    static constexpr int BK = 64;           // fp16 per 128-B swizzle row
+    static constexpr int B_ROWS = BN / CG;  // rows of B each CTA loads
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
+    static constexpr int STAGE_TX = CG * (A_BYTES + B_BYTES); // bytes landing per stage
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, BN);
+    static constexpr int EPI_WARPS = 4;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int STG_BYTES = 32 * 128; // one 32-row × 64-col fp16 box
+};
+
+template <int CG, int STAGES, int EPI> struct SmemLayout {
+    using T = TileCfg<CG>;
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
+    static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
+    static constexpr int EPI_BYTES = (EPI == kEpiTmaF16) ? T::EPI_WARPS * 2 * T::STG_BYTES : 0;
+    static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+    static constexpr int SLOT_OFF = BAR_OFF + 8 * NUM_BARS;
+    static constexpr int ABORT_OFF = SLOT_OFF + 4;
+    static constexpr int BYTES = ABORT_OFF + 4;
+    static constexpr int DYN_BYTES = BYTES + 1024; // slack for 1024-B alignment
+};
+
+__device__ unsigned int vg_status_word;
+
+__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                       unsigned long long timeout_ns, unsigned code) {
+    const uint64_t t0 = ptx::global_timer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 128; ++i)
+            if (ptx::mbar_try_wait(bar, parity))
+                return true;
+        if (*abort_flag)
+            return false;
+        if (ptx::global_timer_ns() - t0 > timeout_ns) {
+            *abort_flag = 1;
+            atomicCAS(&vg_status_word, 0u, code);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                         unsigned long long timeout_ns, unsigned code) {
+    if (ptx::mbar_try_wait(bar, parity))
+        return true;
+    return wait_slow(bar, parity, abort_flag, timeout_ns, code);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(uint32_t lo_bits, uint32_t hi_bits) {
+    __half2 h = __floats2half2_rn(__uint_as_float(lo_bits), __uint_as_float(hi_bits));
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int CG, int STAGES, int EPI>
+__global__ void __launch_bounds__(TileCfg<CG>::THREADS, 1)
+    gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
+                     const __grid_constant__ CUtensorMap mapB,
+                     const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+    using T = TileCfg<CG>;
+    using L = SmemLayout<CG, STAGES, EPI>;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = ptx::smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *const base_ptr = smem_raw + (base - raw);
+
+    const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    const uint32_t rank = (CG == 2) ? ptx::cluster_ctarank() : 0u;
+
+    const uint32_t sA = base + L::A_OFF;
+    const uint32_t sB = base + L::B_OFF;
+    const uint32_t sEpi = base + L::EPI_OFF;
+    const uint32_t sBar = base + L::BAR_OFF;
+    const uint32_t slot = base + L::SLOT_OFF;
+    volatile uint32_t *slot_ptr = reinterpret_cast<volatile uint32_t *>(base_ptr + L::SLOT_OFF);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(base_ptr + L::ABORT_OFF);
+
+    auto full_bar = [&](int s) { return sBar + 8u * s; };
+    auto empty_bar = [&](int s) { return sBar + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return sBar + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return sBar + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(full_bar(s), 1);
+            ptx::mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            ptx::mbar_init(tfull_bar(a), 1);
+            ptx::mbar_init(tempty_bar(a), T::EPI_WARPS * CG);
+        }
+        ptx::mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&mapA);
+        ptx::prefetch_tmap(&mapB);
+        if (EPI == kEpiTmaF16)
+            ptx::prefetch_tmap(&mapC);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc<CG>(slot, T::TMEM_COLS);
+        ptx::tmem_relinquish<CG>();
+    }
+    ptx::tc_fence_before();
+    if constexpr (CG == 2)
+        ptx::cluster_sync();
+    else
+        __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *slot_ptr;
+
+    const int cluster_id = static_cast<int>(blockIdx.x) / CG;
+    const int num_clusters = static_cast<int>(gridDim.x) / CG;
+    const int total_tiles = args.num_m_tiles * args.num_n_tiles;
+    const unsigned long long tmo = args.timeout_ns;
+
+    if (warp == 0) {
+        // ───────────────────────── TMA producer ─────────────────────────
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+                int tm, tn;
+                raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, tm, tn);
+                const int a_row = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM;
+                const int b_row = tn * T::BN + static_cast<int>(rank) * T::B_ROWS;
+                for (int kb = 0; kb < args.num_kb; ++kb) {
+                    if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
+                                  kStatusTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar(stage);
+                    if constexpr (CG == 1) {
+                        ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
+                        ptx::tma_load_2d(sA + stage * T::A_BYTES, &mapA, fb, kb * T::BK, a_row);
+                        ptx::tma_load_2d(sB + stage * T::B_BYTES, &mapB, fb, kb * T::BK, b_row);
+                    } else {
+                        if (rank == 0)
+                            ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
+                        const uint32_t leader_fb = ptx::mapa(fb, 0);
+                        ptx::tma_load_2d_pair(sA + stage * T::A_BYTES, &mapA, leader_fb,
+                                              kb * T::BK, a_row);
+                        ptx::tma_load_2d_pair(sB + stage * T::B_BYTES, &mapB, leader_fb,
+                                              kb * T::BK, b_row);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: the most recent phase issued on each stage must have landed before
+            // this CTA may exit (already true on the normal path; bounded otherwise).
+            if ((CG == 1 || rank == 0) && !ok) {
+                const int n = issued < STAGES ? issued : STAGES;
+                for (int i = 0; i < n; ++i) {
+                    int s = stage - 1 - i;
+                    uint32_t ph = phase;
+                    if (s < 0) {
+                        s += STAGES;
+                        ph ^= 1u;
+                    }
+                    if (!ptx::mbar_try_wait(full_bar(s), ph)) {
+                        const uint64_t t0 = ptx::global_timer_ns();
+                        while (!ptx::mbar_try_wait(full_bar(s), ph) &&
+                               ptx::global_timer_ns() - t0 < tmo) {
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ───────────────────────── MMA issuer ─────────────────────────
+        if (rank == 0 && lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool any = false;
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+                if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
+                              kStatusTimeoutMma)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::BN);
+                for (int kb = 0; kb < args.num_kb; ++kb) {
+                    if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
+                    const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < T::BK / 16; ++k) {
+                        // +32 B per 16-element K step = +2 in the start-address field.
+                        ptx::mma_f16<CG>(d, a0 + 2u * k, b0 + 2u * k, T::IDESC,
+                                         (kb | k) != 0 ? 1u : 0u);
+                    }
+                    any = true;
+                    if constexpr (CG == 1)
+                        ptx::mma_commit(empty_bar(stage));
+                    else
+                        ptx::mma_commit_pair(empty_bar(stage), 0x3);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                if constexpr (CG == 1)
+                    ptx::mma_commit(tfull_bar(acc));
+                else
+                    ptx::mma_commit_pair(tfull_bar(acc), 0x3);
+                acc ^= 1;
+                if (acc == 0)
+                    acc_phase ^= 1u;
+            }
+            // Every MMA issued by this thread must complete before TMEM is freed.
+            if (any) {
+                if constexpr (CG == 1)
+                    ptx::mma_commit(drain_bar);
+                else
+                    ptx::mma_commit_pair(drain_bar, 0x1);
+                if (!ptx::mbar_try_wait(drain_bar, 0)) {
+                    const uint64_t t0 = ptx::global_timer_ns();
+                    while (!ptx::mbar_try_wait(drain_bar, 0)) {
+                        if (ptx::global_timer_ns() - t0 > tmo) {
+                            atomicCAS(&vg_status_word, 0u, (unsigned)kStatusTimeoutDrain);
+                            break;
+                        }
+                    }
+                }
+            }
+        }
+    } else {
+        // ───────────────────────── epilogue ─────────────────────────
+        const int sub = warp & 3;    // TMEM sub-partition this warp may read
+        const int ew = warp - 2;     // staging-buffer owner index
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int buf = 0;
+        for (int t = cluster_id; t < total_tiles; t += num_clusters) {
+            int tm, tn;
+            raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, tm, tn);
+            if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue))
+                break;
+            ptx::tc_fence_after();
+            const int row0 = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
+            const int col0 = tn * T::BN;
+            const uint32_t t_row =
+                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::BN);
+#pragma unroll 1
+            for (int c = 0; c < T::BN / 64; ++c) {
+                uint32_t v0[32], v1[32];
+                ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
+                ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
+                ptx::tmem_wait_ld();
+                if (c == T::BN / 64 - 1) {
+                    // Accumulator buffer fully read: hand it back to the MMA issuer.
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (CG == 1)
+                            ptx::mbar_arrive(tempty_bar(acc));
+                        else
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(acc), 0));
+                    }
+                }
+                const int ccol = col0 + c * 64;
+                if constexpr (EPI == kEpiTmaF16) {
+                    uint32_t p[32];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
+                        p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
+                    }
+                    const uint32_t stg = sEpi + static_cast<uint32_t>((ew * 2 + buf) * T::STG_BYTES);
+                    if (lane == 0)
+                        ptx::bulk_wait_group_read<1>();
+                    __syncwarp();
+                    const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                                     "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
+                                     "r"(p[4 * j + 3])
+                                     : "memory");
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (row0 < args.M && ccol < args.N)
+                            ptx::tma_store_2d(&mapC, stg, ccol, row0);
+                        ptx::bulk_commit_group();
+                    }
+                    buf ^= 1;
+                } else if constexpr (EPI == kEpiDirectF16) {
+                    const int row = row0 + lane;
+                    if (row < args.M) {
+                        __half *crow = static_cast<__half *>(args.C) + static_cast<long long>(row) * args.ldc;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
+                            const int col = ccol + 8 * j;
+                            if (args.c_vec_ok && col + 8 <= args.N) {
+                                uint4 q;
+                                q.x = pack_half2(v[0], v[1]);
+                                q.y = pack_half2(v[2], v[3]);
+                                q.z = pack_half2(v[4], v[5]);
+                                q.w = pack_half2(v[6], v[7]);
+                                *reinterpret_cast<uint4 *>(crow + col) = q;
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e)
+                                    if (col + e < args.N)
+                                        crow[col + e] = __float2half_rn(__uint_as_float(v[e]));
+                            }
+                        }
+                    }
+                } else {
+                    const int row = row0 + lane;
+                    if (row < args.M) {
+                        float *crow = static_cast<float *>(args.C) + static_cast<long long>(row) * args.ldc;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
+                            const int col = ccol + 8 * j;
+                            if (args.c_vec_ok && col + 8 <= args.N) {
+                                float4 q0 = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]),
+                                                        __uint_as_float(v[2]), __uint_as_float(v[3]));
+                                float4 q1 = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]),
+                                                        __uint_as_float(v[6]), __uint_as_float(v[7]));
+                                *reinterpret_cast<float4 *>(crow + col) = q0;
+                                *reinterpret_cast<float4 *>(crow + col + 4) = q1;
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e)
+                                    if (col + e < args.N)
+                                        crow[col + e] = __uint_as_float(v[e]);
+                            }
+                        }
+                    }
+                }
+            }
+            acc ^= 1;
+            if (acc == 0)
+                acc_phase ^= 1u;
+        }
+        if constexpr (EPI == kEpiTmaF16) {
+            if (lane == 0)
+                ptx::bulk_wait_group<0>();
+        }
+        ptx::tc_fence_before();
+    }
+
+    // ───────────────────────── teardown ─────────────────────────
+    __syncthreads();
+    if constexpr (CG == 2)
+        ptx::cluster_sync();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc<CG>(tmem_base, T::TMEM_COLS);
+    }
+#endif
+}
+
+// Failure-detection self test: one CTA waits, with the same bounded wait the GEMM
+// uses, on an mbarrier that nothing ever arrives on, and must come back with
+// kStatusTimeoutSelftest recorded instead of hanging.
+__global__ void wait_timeout_selftest(unsigned long long timeout_ns, unsigned *out_ok) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(ptx::smem_u32(&bar), 1);
+        abort_flag = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = wait_bar(ptx::smem_u32(&bar), 0, &abort_flag, timeout_ns,
+                                 kStatusTimeoutSelftest);
+        *out_ok = ok ? 1u : 0u;
+    }
+#endif
+}
+
+} // namespace vg

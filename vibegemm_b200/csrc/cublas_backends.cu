@@ -1,0 +1,104 @@
+// cuBLAS backend — the engine's reference and the performance yardstick.
+//
+// Registered at priority 0 so the engine uses it as the reference
+// (csrc/cublas_backends.cu:12-44 of VibeGEMM). The reference selects the operand
+// order per target (:24-31); the B200 build uses the row-major-C order of its A100
+// branch (:28-31): C^T = B^T·A in column-major terms, i.e.
+//   cublasGemmEx(T, N, N, M, K, B, K, A, K, C, N), fp16 in/out, CUBLAS_COMPUTE_32F.
+// Failures are reported instead of terminating the process (the reference exits),
+// because this backend also lives inside a shared library loaded by test runners.
+#include <cublas_v2.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "backend.cuh"
+#include "registry.cuh"
+#include "utils.cuh"
+#include "vibegemm_b200.h"
+
+#if !defined(HAS_B200) && !defined(HAS_H100) && !defined(HAS_A100)
+#error "Define one of HAS_B200, HAS_H100, HAS_A100"
+#endif
+
+namespace {
+
+cublasStatus_t gemm_ex(cublasHandle_t h, const half *A, const half *B, half *C, int M, int N,
+                       int K) {
+    const float alpha = 1.f, beta = 0.f;
+#if defined(HAS_H100) && !defined(HAS_B200)
+    // Column-major C (the H100 family's layout).
+    return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, M, N, K, &alpha, A, CUDA_R_16F, K, B, CUDA_R_16F,
+                        K, &beta, C, CUDA_R_16F, M, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+#else
+    // Row-major C (A100 and B200 families).
+    return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, B, CUDA_R_16F, K, A, CUDA_R_16F,
+                        K, &beta, C, CUDA_R_16F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+#endif
+}
+
+} // namespace
+
+class CublasBackend : public GemmBackend {
+  public:
+    CublasBackend() {
+        if (cublasCreate(&handle_) != CUBLAS_STATUS_SUCCESS) {
+            std::fprintf(stderr, "cuBLAS: cublasCreate failed; backend unavailable\n");
+            handle_ = nullptr;
+        }
+    }
+    ~CublasBackend() override {
+        if (handle_)
+            cublasDestroy(handle_);
+    }
+
+    void run(half *A, half *B, half *C, int M, int N, int K) override {
+        if (!handle_)
+            return;
+        const cublasStatus_t s = gemm_ex(handle_, A, B, C, M, N, K);
+        if (s != CUBLAS_STATUS_SUCCESS)
+            std::fprintf(stderr, "cuBLAS error: cublasGemmEx status=%d\n", (int)s);
+    }
+
+    std::string name() const override { return "cuBLAS"; }
+    void teardown() override {}
+    bool is_available() const override { return handle_ != nullptr; }
+
+  private:
+    cublasHandle_t handle_ = nullptr;
+};
+
+REGISTER_CUBLAS("cuBLAS", CublasBackend);
+
+// C ABI: one cuBLAS handle per (thread, device), stream set per call.
+// Returns 0, a cudaError_t code, or 1000 + cublasStatus_t for a cuBLAS failure.
+extern "C" int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
+                                  vg_stream_t stream) {
+    if (M < 0 || N < 0 || K < 0)
+        return (int)cudaErrorInvalidValue;
+    if (M == 0 || N == 0)
+        return 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return (int)e;
+    constexpr int kMaxDev = 64;
+    thread_local cublasHandle_t handles[kMaxDev] = {};
+    if (dev < 0 || dev >= kMaxDev)
+        return (int)cudaErrorInvalidDevice;
+    if (!handles[dev]) {
+        const cublasStatus_t s = cublasCreate(&handles[dev]);
+        if (s != CUBLAS_STATUS_SUCCESS) {
+            handles[dev] = nullptr;
+            return 1000 + (int)s;
+        }
+    }
+    cublasStatus_t s = cublasSetStream(handles[dev], (cudaStream_t)stream);
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = gemm_ex(handles[dev], static_cast<const half *>(A), static_cast<const half *>(B),
+                    static_cast<half *>(C), M, N, K);
+    return s == CUBLAS_STATUS_SUCCESS ? 0 : 1000 + (int)s;
+}

@@ -1,0 +1,581 @@
+// Host side of the B200 FP16 GEMM: launch planning, TMA descriptors, the kernel
+// version ladder and the C ABI declared in include/vibegemm_b200.h.
+//
+// Version ladder (each rung is a registered backend, following the reference's own
+// methodology of keeping every kernel version in the registry,
+// csrc/gemm_h100_backends.cu:56-117):
+//   v0  1 CTA, 128×256 tile, one tile per CTA, direct global stores.
+//   v1  1 CTA, persistent grid (one CTA per SM), grouped raster, TMEM double buffer,
+//       TMA-store epilogue.
+//   v2  CTA pair (tcgen05 cta_group::2), 256×256 tile, 6-stage ring, persistent
+//       clusters, grouped raster, TMEM double buffer, TMA-store epilogue. Default.
+//
+// Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
+// strides: when A or B (K % 8 != 0 or a misaligned pointer) cannot be described,
+// a pre-pass copies it into a K-padded workspace from the stream-ordered pool;
+// when C cannot be (N % 8 != 0 or misaligned), the epilogue switches to predicated
+// direct stores. Partial tiles use TMA out-of-bounds zero fill and store clipping.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "b200/gemm_kernel.cuh"
+#include "b200/schedule.cuh"
+#include "vibegemm_b200.h"
+
+namespace vg {
+namespace {
+
+struct VersionDesc {
+    const char *name;
+    int cta_group;
+    int stages;
+    bool persistent;
+    bool tma_store;
+    int group_m;
+};
+
+constexpr VersionDesc kVersions[] = {
+    {"VibeGEMM B200 v0", 1, 4, false, false, 8},
+    {"VibeGEMM B200 v1", 1, 4, true, true, 8},
+    {"VibeGEMM B200 v2", 2, 6, true, true, 8},
+};
+constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
+constexpr int kDefaultVersion = 2;
+constexpr int kMaxDevices = 64;
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
+
+struct Plan {
+    int cta_group = 1;
+    int stages = 4;
+    int epi = kEpiTmaF16;
+    int pad_a = 0, pad_b = 0;
+    int Kp = 0;
+    int num_m_tiles = 0, num_n_tiles = 0, num_kb = 0;
+    int group_m = 8;
+    int grid = 0;
+    int persistent = 0;
+};
+
+inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
+
+// Pure host planning (no CUDA calls): what the launcher will do for this problem.
+int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C, bool f32_out,
+              int num_sms, int max_clusters, Plan &p) {
+    if (version < 0 || version >= kNumVersions || M < 0 || N < 0 || K < 0 || num_sms <= 0)
+        return cudaErrorInvalidValue;
+    const VersionDesc &v = kVersions[version];
+    p = Plan{};
+    p.cta_group = v.cta_group;
+    p.stages = v.stages;
+    p.group_m = v.group_m;
+    p.persistent = v.persistent ? 1 : 0;
+    p.pad_a = (K % 8 != 0) || !aligned16(A);
+    p.pad_b = (K % 8 != 0) || !aligned16(B);
+    p.Kp = (K % 8 == 0) ? K : (K + 7) / 8 * 8;
+    if (f32_out)
+        p.epi = kEpiDirectF32;
+    else if (v.tma_store && N % 8 == 0 && aligned16(C))
+        p.epi = kEpiTmaF16;
+    else
+        p.epi = kEpiDirectF16;
+    p.num_m_tiles = ceil_div_i(M, 128 * v.cta_group);
+    p.num_n_tiles = ceil_div_i(N, 256);
+    p.num_kb = ceil_div_i(p.Kp, 64);
+    const long long tiles = (long long)p.num_m_tiles * p.num_n_tiles;
+    if (v.persistent) {
+        const int slots = (v.cta_group == 2) ? std::max(1, max_clusters) : num_sms;
+        p.grid = (int)std::min<long long>(tiles, slots) * v.cta_group;
+    } else {
+        p.grid = (int)tiles * v.cta_group;
+    }
+    return cudaSuccess;
+}
+
+// ── per-device facts ─────────────────────────────────────────────────────────
+struct DeviceInfo {
+    int num_sms = 0;
+    int major = 0, minor = 0;
+    bool ok = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+const DeviceInfo *device_info(int dev) {
+    if (dev < 0 || dev >= kMaxDevices)
+        return nullptr;
+    std::call_once(g_dev_once[dev], [dev] {
+        DeviceInfo &d = g_dev[dev];
+        if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return;
+        }
+        d.ok = true;
+    });
+    return &g_dev[dev];
+}
+
+std::atomic<unsigned long long> g_timeout_ns{0};
+
+unsigned long long wait_timeout_ns() {
+    unsigned long long t = g_timeout_ns.load(std::memory_order_relaxed);
+    if (t == 0) {
+        t = kDefaultTimeoutNs;
+        if (const char *env = std::getenv("VG_WAIT_TIMEOUT_MS")) {
+            const long long ms = std::atoll(env);
+            if (ms > 0)
+                t = (unsigned long long)ms * 1000000ull;
+        }
+        g_timeout_ns.store(t, std::memory_order_relaxed);
+    }
+    return t;
+}
+
+// ── TMA descriptors ──────────────────────────────────────────────────────────
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            (void)cudaGetLastError();
+            p = nullptr;
+        }
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+struct MapKey {
+    const void *base;
+    uint64_t cols, rows, ld;
+    uint32_t box_cols, box_rows;
+    int dev;
+    bool operator==(const MapKey &o) const {
+        return base == o.base && cols == o.cols && rows == o.rows && ld == o.ld &&
+               box_cols == o.box_cols && box_rows == o.box_rows && dev == o.dev;
+    }
+};
+
+struct MapCache {
+    static constexpr int kSize = 16;
+    MapKey key[kSize];
+    CUtensorMap map[kSize];
+    int used = 0, next = 0;
+    void clear() { used = next = 0; }
+};
+thread_local MapCache t_maps;
+
+// Row-major fp16 matrix of `rows` × `cols` with row stride `ld` elements, loaded or
+// stored in boxes of box_rows × box_cols with 128-B swizzle (box_cols·2 = 128 B).
+// Out-of-range elements read as zero and are clipped on store.
+bool get_map(CUtensorMap &out, const void *base, uint64_t cols, uint64_t rows, uint64_t ld,
+             uint32_t box_cols, uint32_t box_rows, int dev) {
+    const MapKey k{base, cols, rows, ld, box_cols, box_rows, dev};
+    for (int i = 0; i < t_maps.used; ++i)
+        if (t_maps.key[i] == k) {
+            out = t_maps.map[i];
+            return true;
+        }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn)
+        return false;
+    CUtensorMap m;
+    std::memset(&m, 0, sizeof(m));
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * sizeof(__half)};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t elem_strides[2] = {1, 1};
+    const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                          strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return false;
+    const int slot = t_maps.next;
+    t_maps.key[slot] = k;
+    t_maps.map[slot] = m;
+    t_maps.next = (slot + 1) % MapCache::kSize;
+    t_maps.used = std::min(t_maps.used + 1, MapCache::kSize);
+    out = m;
+    return true;
+}
+
+// ── pad pre-pass ─────────────────────────────────────────────────────────────
+// dst[r, 0:ld_dst] = src[r, 0:cols] followed by zeros; ld_dst % 8 == 0, dst 16-B
+// aligned. One thread writes one 16-B group; reads are coalesced 2-B loads (src
+// may be arbitrarily aligned).
+__global__ void pad_rows_f16(const __half *__restrict__ src, long long rows, int cols,
+                             long long ld_src, __half *__restrict__ dst, int ld_dst) {
+    const long long groups_per_row = ld_dst / 8;
+    const long long total = rows * groups_per_row;
+    const unsigned short *s16 = reinterpret_cast<const unsigned short *>(src);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / groups_per_row;
+        const int c0 = (int)(i - r * groups_per_row) * 8;
+        const unsigned short *row = s16 + r * ld_src;
+        unsigned short v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            v[e] = (c0 + e < cols) ? row[c0 + e] : (unsigned short)0;
+        uint4 q;
+        q.x = v[0] | ((unsigned)v[1] << 16);
+        q.y = v[2] | ((unsigned)v[3] << 16);
+        q.z = v[4] | ((unsigned)v[5] << 16);
+        q.w = v[6] | ((unsigned)v[7] << 16);
+        *reinterpret_cast<uint4 *>(dst + r * ld_dst + c0) = q;
+    }
+}
+
+cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, int ld_dst,
+                       int num_sms, cudaStream_t s) {
+    if (rows == 0)
+        return cudaSuccess;
+    const long long total = rows * (ld_dst / 8);
+    const int threads = 256;
+    const long long want = (total + threads - 1) / threads;
+    const int blocks = (int)std::min<long long>(want, (long long)num_sms * 8);
+    pad_rows_f16<<<blocks, threads, 0, s>>>(static_cast<const __half *>(src), rows, cols, cols, dst,
+                                            ld_dst);
+    return cudaGetLastError();
+}
+
+// ── kernel launch ────────────────────────────────────────────────────────────
+template <int CG, int STAGES, int EPI> struct Inst {
+    static constexpr int kSmem = SmemLayout<CG, STAGES, EPI>::DYN_BYTES;
+    static std::atomic<unsigned long long> attr_ready; // bit per device
+    static int max_clusters[kMaxDevices];
+
+    static cudaError_t prepare(int dev) {
+        if ((attr_ready.load(std::memory_order_acquire) >> dev) & 1ull)
+            return cudaSuccess;
+        auto kern = &gemm_f16_tcgen05<CG, STAGES, EPI>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess)
+            return e;
+        int clusters = 0;
+        if (CG == 2) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(2 * 1024, 1, 1);
+            cfg.blockDim = dim3(TileCfg<CG>::THREADS, 1, 1);
+            cfg.dynamicSmemBytes = kSmem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+            if (e != cudaSuccess)
+                return e;
+        }
+        max_clusters[dev] = clusters;
+        attr_ready.fetch_or(1ull << dev, std::memory_order_acq_rel);
+        return cudaSuccess;
+    }
+
+    static cudaError_t launch(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
+                              const GemmArgs &args, int grid, cudaStream_t s) {
+        auto kern = &gemm_f16_tcgen05<CG, STAGES, EPI>;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid, 1, 1);
+        cfg.blockDim = dim3(TileCfg<CG>::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = kSmem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        if (CG == 2) {
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+        }
+        return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
+    }
+};
+template <int CG, int STAGES, int EPI> std::atomic<unsigned long long> Inst<CG, STAGES, EPI>::attr_ready{0};
+template <int CG, int STAGES, int EPI> int Inst<CG, STAGES, EPI>::max_clusters[kMaxDevices] = {};
+
+template <int CG, int STAGES>
+cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
+                         const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
+                         const GemmArgs *args, int grid, cudaStream_t s) {
+#define VG_EPI_CASE(E)                                                                             \
+    case E: {                                                                                      \
+        cudaError_t e = Inst<CG, STAGES, E>::prepare(dev);                                         \
+        if (e != cudaSuccess)                                                                      \
+            return e;                                                                              \
+        max_clusters = Inst<CG, STAGES, E>::max_clusters[dev];                                     \
+        if (query_only)                                                                            \
+            return cudaSuccess;                                                                    \
+        return Inst<CG, STAGES, E>::launch(*ma, *mb, *mc, *args, grid, s);                         \
+    }
+    switch (epi) {
+        VG_EPI_CASE(kEpiTmaF16)
+        VG_EPI_CASE(kEpiDirectF16)
+        VG_EPI_CASE(kEpiDirectF32)
+    default:
+        return cudaErrorInvalidValue;
+    }
+#undef VG_EPI_CASE
+}
+
+cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
+                     const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
+                     const GemmArgs *args, int grid, cudaStream_t s) {
+    if (p.cta_group == 1 && p.stages == 4)
+        return dispatch_epi<1, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    if (p.cta_group == 2 && p.stages == 6)
+        return dispatch_epi<2, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
+                     bool f32_out, cudaStream_t s) {
+    if (version < 0 || version >= kNumVersions || M < 0 || N < 0 || K < 0)
+        return cudaErrorInvalidValue;
+    if (M == 0 || N == 0)
+        return cudaSuccess;
+    if (!A || !B || !C)
+        return cudaErrorInvalidValue;
+    const size_t out_elt = f32_out ? sizeof(float) : sizeof(__half);
+    if (K == 0)
+        return cudaMemsetAsync(C, 0, (size_t)M * N * out_elt, s);
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    const DeviceInfo *di = device_info(dev);
+    if (!di || !di->ok)
+        return cudaErrorInvalidDevice;
+    if (di->major != 10 || di->minor != 0)
+        return cudaErrorNoKernelImageForDevice;
+
+    Plan p;
+    e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, f32_out,
+                               di->num_sms, di->num_sms / 2, p);
+    if (e != cudaSuccess)
+        return e;
+
+    // Occupancy-limited cluster count for the persistent pair kernel.
+    int max_clusters = 0;
+    e = dispatch(p, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
+    if (e != cudaSuccess)
+        return e;
+    int grid = p.grid;
+    if (p.cta_group == 2 && p.persistent && max_clusters > 0)
+        grid = std::min(grid, 2 * max_clusters);
+
+    // Operands TMA cannot describe go through a K-padded copy.
+    const void *A_use = A, *B_use = B;
+    void *ws = nullptr;
+    const int Kp = p.Kp;
+    if (p.pad_a || p.pad_b) {
+        const size_t a_bytes = p.pad_a ? (size_t)M * Kp * sizeof(__half) : 0;
+        const size_t b_bytes = p.pad_b ? (size_t)N * Kp * sizeof(__half) : 0;
+        e = cudaMallocAsync(&ws, a_bytes + b_bytes, s);
+        if (e != cudaSuccess)
+            return e;
+        __half *wa = static_cast<__half *>(ws);
+        __half *wb = reinterpret_cast<__half *>(static_cast<char *>(ws) + a_bytes);
+        if (p.pad_a) {
+            e = launch_pad(A, M, K, wa, Kp, di->num_sms, s);
+            A_use = wa;
+        }
+        if (e == cudaSuccess && p.pad_b) {
+            e = launch_pad(B, N, K, wb, Kp, di->num_sms, s);
+            B_use = wb;
+        }
+        if (e != cudaSuccess) {
+            (void)cudaFreeAsync(ws, s);
+            return e;
+        }
+    }
+
+    CUtensorMap ma, mb, mc;
+    std::memset(&mc, 0, sizeof(mc));
+    const uint32_t b_box_rows = (p.cta_group == 2) ? 128u : 256u;
+    bool ok = get_map(ma, A_use, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp, 64u, 128u, dev) &&
+              get_map(mb, B_use, (uint64_t)Kp, (uint64_t)N, (uint64_t)Kp, 64u, b_box_rows, dev);
+    if (ok && p.epi == kEpiTmaF16)
+        ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
+    if (!ok) {
+        if (ws)
+            (void)cudaFreeAsync(ws, s);
+        return cudaErrorInvalidValue;
+    }
+
+    GemmArgs args{};
+    args.M = M;
+    args.N = N;
+    args.K = Kp;
+    args.num_m_tiles = p.num_m_tiles;
+    args.num_n_tiles = p.num_n_tiles;
+    args.num_kb = p.num_kb;
+    args.group_m = p.group_m;
+    args.c_vec_ok = (N % (f32_out ? 4 : 8) == 0) && aligned16((uintptr_t)C);
+    args.C = C;
+    args.ldc = N;
+    args.timeout_ns = wait_timeout_ns();
+
+    e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+    if (ws) {
+        const cudaError_t f = cudaFreeAsync(ws, s);
+        if (e == cudaSuccess)
+            e = f;
+    }
+    return e;
+}
+
+} // namespace
+} // namespace vg
+
+// ── C ABI ────────────────────────────────────────────────────────────────────
+extern "C" {
+
+int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C, int M, int N,
+                             int K, vg_stream_t stream) {
+    return (int)vg::run_gemm(version, A, B, C, M, N, K, false, (cudaStream_t)stream);
+}
+
+int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
+                     vg_stream_t stream) {
+    return (int)vg::run_gemm(vg::kDefaultVersion, A, B, C, M, N, K, false, (cudaStream_t)stream);
+}
+
+int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C, int M, int N,
+                            int K, vg_stream_t stream) {
+    return (int)vg::run_gemm(version, A, B, C, M, N, K, true, (cudaStream_t)stream);
+}
+
+int vg_b200_num_versions(void) { return vg::kNumVersions; }
+
+const char *vg_b200_version_name(int version) {
+    if (version < 0 || version >= vg::kNumVersions)
+        return nullptr;
+    return vg::kVersions[version].name;
+}
+
+int vg_b200_default_version(void) { return vg::kDefaultVersion; }
+
+int vg_b200_is_available(int device) {
+    const vg::DeviceInfo *di = vg::device_info(device);
+    if (!di || !di->ok || di->major != 10 || di->minor != 0)
+        return 0;
+    cudaFuncAttributes fa;
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    const cudaError_t e = cudaFuncGetAttributes(&fa, vg::gemm_f16_tcgen05<2, 6, vg::kEpiTmaF16>);
+    if (prev != device)
+        (void)cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return 1;
+}
+
+void vg_b200_teardown(void) { vg::t_maps.clear(); }
+
+unsigned vg_b200_device_status(int reset) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, vg::vg_status_word, sizeof(v)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0xFFFFFFFFu;
+    }
+    if (reset) {
+        const unsigned zero = 0;
+        if (cudaMemcpyToSymbol(vg::vg_status_word, &zero, sizeof(zero)) != cudaSuccess)
+            (void)cudaGetLastError();
+    }
+    return v;
+}
+
+int vg_b200_set_wait_timeout_ns(unsigned long long ns) {
+    vg::g_timeout_ns.store(ns == 0 ? vg::kDefaultTimeoutNs : ns, std::memory_order_relaxed);
+    return 0;
+}
+
+int vg_b200_selftest_wait_timeout(unsigned long long timeout_ns) {
+    unsigned *d_ok = nullptr;
+    if (cudaMalloc(&d_ok, sizeof(unsigned)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    const unsigned sentinel = 7;
+    int result = 0;
+    (void)vg_b200_device_status(1);
+    if (cudaMemcpy(d_ok, &sentinel, sizeof(unsigned), cudaMemcpyHostToDevice) == cudaSuccess) {
+        vg::wait_timeout_selftest<<<1, 32>>>(timeout_ns, d_ok);
+        unsigned ok = sentinel;
+        if (cudaDeviceSynchronize() == cudaSuccess &&
+            cudaMemcpy(&ok, d_ok, sizeof(unsigned), cudaMemcpyDeviceToHost) == cudaSuccess) {
+            const unsigned status = vg_b200_device_status(1);
+            result = (ok == 0u && status == (unsigned)vg::kStatusTimeoutSelftest) ? 1 : 0;
+        }
+    }
+    (void)cudaGetLastError();
+    cudaFree(d_ok);
+    return result;
+}
+
+void vg_shard_rows(long long M, int world, int rank, long long *row0, long long *rows) {
+    long long r0 = 0, n = 0;
+    if (world > 0 && rank >= 0 && rank < world && M > 0)
+        vg::shard_rows(M, world, rank, r0, n);
+    if (row0)
+        *row0 = r0;
+    if (rows)
+        *rows = n;
+}
+
+void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *tile_n) {
+    int tm = -1, tn = -1;
+    if (num_m > 0 && num_n > 0 && group_m > 0 && t >= 0 && t < num_m * num_n)
+        vg::raster_tile(t, num_m, num_n, group_m, tm, tn);
+    if (tile_m)
+        *tile_m = tm;
+    if (tile_n)
+        *tile_n = tn;
+}
+
+int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
+                 int f32_out, int num_sms, int *out) {
+    vg::Plan p;
+    const int e = vg::make_plan(version, M, N, K, A, B, C, f32_out != 0, num_sms, num_sms / 2, p);
+    if (e != 0 || !out)
+        return e ? e : (int)cudaErrorInvalidValue;
+    const int vals[12] = {p.cta_group, p.stages,      p.epi,         p.pad_a,
+                          p.pad_b,     p.Kp,          p.num_m_tiles, p.num_n_tiles,
+                          p.num_kb,    p.group_m,     p.grid,        p.persistent};
+    std::memcpy(out, vals, sizeof(vals));
+    return 0;
+}
+
+} // extern "C"

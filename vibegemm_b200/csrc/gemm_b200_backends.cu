@@ -1,0 +1,66 @@
+// B200 backend family: adapts each kernel version's launchKernel to GemmBackend and
+// registers it, exactly as the reference wires its H100 family
+// (csrc/gemm_h100_backends.cu:34-57): a template adapter over a free function
+// void launchKernel(half*, half*, half*, int, int, int), one registration per
+// version, display names "VibeGEMM B200 vN".
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <string>
+
+#include "backend.cuh"
+#include "registry.cuh"
+#include "vibegemm_b200.h"
+
+namespace {
+
+// Launch on the legacy default stream, where the engine records its events
+// (include/engine.cuh timing, include/utils.cuh CudaTimer). Host-side errors
+// (unsupported device, bad sizes) are reported on stderr; device-side errors surface
+// at the engine's next cuda_check().
+template <int V> void launch_version(half *A, half *B, half *C, int M, int N, int K) {
+    const int e = vg_b200_gemm_f16_version(V, A, B, C, M, N, K, nullptr);
+    if (e != 0)
+        std::fprintf(stderr, "VibeGEMM B200 v%d: launch failed: %s\n", V,
+                     cudaGetErrorString((cudaError_t)e));
+}
+
+} // namespace
+
+namespace gemm_b200_v0 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<0>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v0
+namespace gemm_b200_v1 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<1>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v1
+namespace gemm_b200_v2 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<2>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v2
+
+using KernelFn = void (*)(half *, half *, half *, int, int, int);
+
+template <KernelFn Fn> class GeneratedB200KernelBackend : public GemmBackend {
+  public:
+    explicit GeneratedB200KernelBackend(std::string backend_name)
+        : backend_name_(std::move(backend_name)) {}
+
+    void run(half *A, half *B, half *C, int M, int N, int K) override { Fn(A, B, C, M, N, K); }
+    std::string name() const override { return backend_name_; }
+    void teardown() override { vg_b200_teardown(); }
+    bool is_available() const override {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return false;
+        }
+        return vg_b200_is_available(dev) != 0;
+    }
+
+  private:
+    std::string backend_name_;
+};
+
+REGISTER_B200_KERNEL("VibeGEMM B200 v0", GeneratedB200KernelBackend<gemm_b200_v0::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v1", GeneratedB200KernelBackend<gemm_b200_v1::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v2", GeneratedB200KernelBackend<gemm_b200_v2::launchKernel>);

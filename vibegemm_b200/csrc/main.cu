@@ -1,0 +1,114 @@
+// VibeGEMM driver: runs every registered backend of this build through the engine.
+//
+// Mirrors the reference driver (main.cu:68-109 of VibeGEMM): query device 0, open
+// the per-architecture log, take KernelRegistry::make_all(), keep the backends of
+// this architecture, run each problem size. The B200 arm (sm >= 100) keeps
+// "B200" backends and cuBLAS, drops "A100"/"H100" names and logs to
+// results/perf_b200.txt. The default problem list is the reference's (8192³);
+// shapes can be given as arguments: `VibeGEMM [--normal] MxNxK ...`
+// (--normal = N(0, 0.02) inputs instead of uniform[-1,1]).
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <sys/stat.h>
+#include <vector>
+
+#include "engine.cuh"
+#include "registry.cuh"
+
+static FILE *g_fp = nullptr;
+
+static void log_print(const char *fmt, ...) {
+    va_list args;
+    va_start(args, fmt);
+    std::vprintf(fmt, args);
+    va_end(args);
+    if (g_fp) {
+        va_start(args, fmt);
+        std::vfprintf(g_fp, fmt, args);
+        va_end(args);
+    }
+}
+
+struct GemmProblem {
+    const char *label;
+    int m, n, k;
+};
+
+static const GemmProblem kDefaultSizes[] = {
+    {nullptr, 8192, 8192, 8192},
+};
+
+int main(int argc, char **argv) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, 0) != cudaSuccess) {
+        std::fprintf(stderr, "no CUDA device\n");
+        return 1;
+    }
+    const int sm = prop.major * 10 + prop.minor;
+
+    std::vector<GemmProblem> sizes;
+    bool normal = false;
+    for (int i = 1; i < argc; ++i) {
+        if (std::strcmp(argv[i], "--normal") == 0) {
+            normal = true;
+            continue;
+        }
+        int m = 0, n = 0, k = 0;
+        if (std::sscanf(argv[i], "%dx%dx%d", &m, &n, &k) == 3 && m > 0 && n > 0 && k > 0)
+            sizes.push_back({nullptr, m, n, k});
+        else {
+            std::fprintf(stderr, "bad shape '%s' (expected MxNxK)\n", argv[i]);
+            return 2;
+        }
+    }
+    if (sizes.empty())
+        sizes.assign(std::begin(kDefaultSizes), std::end(kDefaultSizes));
+
+    mkdir("results", 0755);
+    const std::string log_file = (sm >= 100)  ? "results/perf_b200.txt"
+                                 : (sm >= 90) ? "results/perf_h100.txt"
+                                              : "results/perf_a100.txt";
+    g_fp = std::fopen(log_file.c_str(), "w");
+    if (!g_fp) {
+        std::fprintf(stderr, "Failed to open %s for writing!\n", log_file.c_str());
+        return 1;
+    }
+    log_print("=== Device: %s (SM: %d) ===\n", prop.name, sm);
+
+    BenchmarkEngine engine;
+    engine.set_log_file(g_fp);
+    if (normal)
+        engine.set_inputs(BenchmarkEngine::Inputs::Normal002);
+
+    for (auto &b : KernelRegistry::instance().make_all()) {
+        const std::string name = b->name();
+        const bool is_a100 = name.find("A100") != std::string::npos;
+        const bool is_h100 = name.find("H100") != std::string::npos;
+        const bool is_b200 = name.find("B200") != std::string::npos;
+        if (sm >= 100 && (is_a100 || is_h100))
+            continue;
+        if (sm >= 90 && sm < 100 && (is_a100 || is_b200))
+            continue;
+        if (sm < 90 && (is_h100 || is_b200))
+            continue;
+        engine.add_backend(b);
+    }
+
+    int failures = 0;
+    for (const auto &c : sizes) {
+        if (c.label)
+            log_print("\n>>> %s\n", c.label);
+        engine.execute(c.m, c.n, c.k);
+        for (const auto &r : engine.results())
+            if (!r.skipped && (!r.ran || !r.err.passed))
+                ++failures;
+    }
+    log_print("\nDone.\n");
+    std::fflush(g_fp);
+    std::fclose(g_fp);
+    g_fp = nullptr;
+    return failures == 0 ? 0 : 3;
+}
