@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""FP16 GEMM benchmark of the B200 backend (the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step is one C = A·B^T GEMM (fp16 in, fp32 accumulate, fp16 out) of the workload:
+M=N=K=8192 per GPU (the reference's 8192³ headline). With N GPUs (torchrun, one process
+per GPU) A and C are split into contiguous row blocks of 8192 rows per rank and B is
+replicated (weak scaling, no collective in the data path). Rank 0 prints ONE JSON line.
+
+* ``value``      whole-job TFLOP/s, inputs resident in HBM, CUDA events on the launching
+                 stream around exactly K launches, barrier + synchronize on both sides,
+                 max over ranks. A+B+C = 384 MiB per GPU per step > 126 MB L2.
+* ``e2e``        the same metric through the C ABI with pinned HOST buffers: every step
+                 copies A and B host→device, runs the GEMM and copies C device→host.
+* ``cublas``     cublasGemmEx on the same buffers in the same run (the yardstick).
+* ``roofline``   tensor-bound: 2·M·N·K per launch / average launch time vs the measured
+                 dense bf16/fp16 peak (MEASURED_PEAKS.json), plus DRAM traffic per launch
+                 from the committed ncu summary.
+* ``cpu_baseline`` the CPU oracle (a port of the reference's naive GEMM; the reference has
+                 no host GEMM) on a bounded row sample, rank 0 at N=1 only.
+
+``--impl reference`` times that CPU path alone on the host cores (rank 0; other ranks
+exit 0) and prints the same line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP16 GEMM TFLOP/s @ M=N=K=8192 per B200; % of dense peak; vs cuBLAS"
+UNIT = "TFLOP/s"
+ROWS_PER_GPU, N_DIM, K_DIM = 8192, 8192, 8192
+FALLBACK_PEAK_TFLOPS = 1590.0  # used only when MEASURED_PEAKS.json is absent
+PROFILE_SUMMARY = ROOT / "profiles" / "gemm_b200_v3_8192.md"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--version", type=int, default=None, help="kernel version (default: fastest)")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of C (N>1)")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"tflops": float(d["bf16_tflops"]), "sustained": float(d.get("bf16_tflops_sustained", 0)),
+                "source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)"}
+    return {"tflops": FALLBACK_PEAK_TFLOPS, "sustained": 0.0, "source": "fallback"}
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+    if not PROFILE_SUMMARY.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", PROFILE_SUMMARY.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.h = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            n = pynvml.nvmlDeviceGetCount()
+            for i in range(n):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if uuid.replace("GPU-", "") in u:
+                    self.h = h
+            if self.h is None:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML unavailable: report that instead of clocks
+            self.error = repr(e)
+
+    def _sample(self):
+        try:
+            get_reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.samples.append((self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                 int(get_reasons(self.h))))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.h is not None:
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+
+    def summary(self) -> dict:
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = [name for b, name in self.REASONS.items() if bits & b and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The oracle GEMM (all host threads) on a bounded row sample of the 8192³ problem."""
+    import numpy as np
+    import oracle
+
+    threads = oracle.max_threads()
+    A, B = oracle.make_inputs(64, N_DIM, K_DIM)  # sample rows, full N and K
+    t0 = time.perf_counter()
+    oracle.gemm_f32(A, B, 0, 8, threads)
+    t_cal = max(time.perf_counter() - t0, 1e-3)
+    rows = int(max(8, min(64, 8 * seconds / t_cal)))
+    rows -= rows % 8
+    t0 = time.perf_counter()
+    oracle.gemm_f32(A, B, 0, rows, threads)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * N_DIM * K_DIM
+    del np
+    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rows} of 8192 rows of the 8192x8192x8192 GEMM ({flops:.3g} FLOP, {dt:.2f} s)"}
+
+
+def run_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import oracle
+
+    threads = oracle.max_threads()
+    A, B = oracle.make_inputs(64, N_DIM, K_DIM)
+    t0 = time.perf_counter()
+    oracle.gemm_f32(A, B, 0, 8, threads)
+    per_row = max(time.perf_counter() - t0, 1e-3) / 8
+    budget = 120.0  # seconds for warmup + steps together
+    rows = int(max(8, min(64, budget / max(1, args.steps + args.warmup) / per_row)))
+    rows -= rows % 8
+    for _ in range(args.warmup):
+        oracle.gemm_f32(A, B, 0, rows, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.gemm_f32(A, B, 0, rows, threads)
+    dt = (time.perf_counter() - t0) / max(1, args.steps)
+    value = 2.0 * rows * N_DIM * K_DIM / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": "fp16_gemm_8192x8192x8192", "M": ROWS_PER_GPU, "N": N_DIM, "K": K_DIM,
+                       "step": f"{rows}-row sample of the workload per step"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{rows} of 8192 rows per step (CPU oracle: the reference has no host GEMM)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import vibegemm_b200 as vg
+    from vibegemm_b200.mgpu import RowShardedGemm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    assert vg.is_available(local), "not an sm_100 B200 device"
+    version = vg.default_version() if args.version is None else args.version
+    M = ROWS_PER_GPU * world
+    sh = RowShardedGemm(M, N_DIM, K_DIM, rank, world)
+    r0, rows = sh.local
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(42 + rank)
+    A = torch.empty((rows, K_DIM), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=gen)
+    gen.manual_seed(77)
+    B = torch.empty((N_DIM, K_DIM), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=gen)
+    C = torch.empty((rows, N_DIM), dtype=torch.float16, device="cuda")
+    Cref = torch.empty_like(C)
+    plan = vg.plan(version, rows, N_DIM, K_DIM, A.data_ptr(), B.data_ptr(), C.data_ptr(),
+                   num_sms=torch.cuda.get_device_properties(local).multi_processor_count)
+    launches_per_gemm = 1 + plan["pad_a"] + plan["pad_b"]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        vg.gemm(A, B, out=C, version=version, stream=stream)
+
+    def timed(fn, steps, warmup, sampler=None):
+        for _ in range(warmup):
+            fn()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if sampler:
+            sampler.start()
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        if sampler:
+            sampler.stop()
+        barrier()
+        return e0.elapsed_time(e1) / steps
+
+    sampler = ClockSampler(local)
+    ms_local = timed(step, args.steps, max(3, args.warmup), sampler)
+    ms = max_over_ranks(ms_local)
+    flop_step = 2.0 * M * N_DIM * K_DIM
+    value = flop_step / (ms * 1e-3) / 1e12
+    status = vg.device_status()
+
+    # cuBLAS yardstick on the same buffers.
+    ms_cublas = max_over_ranks(timed(lambda: vg.cublas_gemm(A, B, out=Cref, stream=stream),
+                                     args.steps, max(3, args.warmup)))
+    # Correctness of the timed kernel against cuBLAS (the reference engine's criterion).
+    step()
+    torch.cuda.synchronize()
+    diff = (C.float() - Cref.float()).abs()
+    bad = int((diff > 1e-3 + 1e-2 * Cref.float().abs()).sum().item())
+    check = {"vs": "cuBLAS", "max_abs": float(diff.max().item()), "mismatches": bad, "passed": bad == 0}
+
+    # End to end through the C ABI with pinned host buffers.
+    hA = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
+    hB = torch.empty(B.shape, dtype=B.dtype, pin_memory=True)
+    hC = torch.empty(C.shape, dtype=C.dtype, pin_memory=True)
+    hA.copy_(A)
+    hB.copy_(B)
+
+    def e2e_step():
+        A.copy_(hA, non_blocking=True)
+        B.copy_(hB, non_blocking=True)
+        vg.gemm(A, B, out=C, version=version, stream=stream)
+        hC.copy_(C, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    ms_e2e = max_over_ranks(timed(e2e_step, e2e_steps, 3))
+    e2e = {"value": flop_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+           "h2d_bytes_per_step": world * (A.numel() + B.numel()) * 2,
+           "d2h_bytes_per_step": world * C.numel() * 2, "ms_per_step": ms_e2e,
+           "path": "vg_b200_gemm_f16 C ABI; pinned host A,B -> HBM, GEMM, C -> pinned host"}
+
+    allgather = None
+    if args.allgather and world > 1:
+        def gather_step():
+            sh.gather(C)
+        ms_ag = max_over_ranks(timed(gather_step, min(args.steps, 20), 3))
+        allgather = {"ms_per_step": ms_ag, "bytes_per_rank": M * N_DIM * 2}
+
+    pk = peaks()
+    per_gpu_launch_tflops = 2.0 * rows * N_DIM * K_DIM / (ms_local * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": per_gpu_launch_tflops, "peak": pk["tflops"], "unit": UNIT,
+            "frac": per_gpu_launch_tflops / pk["tflops"], "traffic": profile_traffic(),
+            "peak_source": pk["source"],
+            "algorithmic": "2*M*N*K FLOP per launch (M=8192 rows of this GPU, N=K=8192)"}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    clocks = sampler.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "accumulate": "f32", "data": "synthetic",
+            "config": {"workload": "fp16_gemm_8192x8192x8192_per_gpu", "M": M, "N": N_DIM, "K": K_DIM,
+                       "rows_per_gpu": ROWS_PER_GPU, "parallelism": f"row-block x{world} (B replicated)",
+                       "layout": "A MxK row-major, B NxK (K contiguous), C MxN row-major",
+                       "inputs": "uniform[-1,1] fp16, seeded device generator",
+                       "l2": "inputs larger than L2 (384 MiB per GPU per step vs 126 MB L2)",
+                       "kernel": vg.versions()[version]},
+            "pct_of_peak": per_gpu_launch_tflops / pk["tflops"],
+            "cublas": {"value": flop_step / (ms_cublas * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_cublas},
+            "pct_of_cublas": ms_cublas / ms,
+            "check": check, "device_status": status,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps * launches_per_gemm,
+            "clocks": clocks,
+        }
+        if allgather:
+            line["allgather"] = allgather
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -59,6 +59,12 @@ int vg_b200_num_versions(void);
 const char *vg_b200_version_name(int version);
 int vg_b200_default_version(void);
 
+/* Tuning: height (in M tiles) of the grouped raster the persistent kernels walk;
+ * 0 restores each version's default. The VG_RASTER_GROUP_M environment variable sets
+ * the initial value. Replaces the compile-time group constants of the reference's
+ * schedulers (csrc/h100/gemm_8192x8192_v18.cuh:207, TM=16). */
+int vg_b200_set_raster_group(int group_m);
+
 /* Replaces GemmBackend::is_available (include/backend.cuh:24): 1 if `device` is an
  * sm_100 part this library was built for, 0 otherwise (never throws). */
 int vg_b200_is_available(int device);
@@ -88,9 +94,9 @@ void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *
 
 /* Host-side launch plan for a problem, as the launcher would build it for a device
  * with `num_sms` SMs (exposed so the planner can be tested without a GPU).
- * Fields of `out` (int[12]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct
+ * Fields of `out` (int[13]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct
  * fp16, 2 direct fp32), pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb,
- * group_m, grid (CTAs), persistent. Returns 0 or a cudaError_t code for bad input. */
+ * group_m, grid (CTAs), persistent, tile columns. Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int f32_out, int num_sms, int *out);
 

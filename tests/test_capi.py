@@ -27,8 +27,9 @@ def test_library_exports_every_declared_symbol(vg):
 
 
 def test_versions_and_registry_order(vg):
-    assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2"]
-    assert vg.default_version() == 2
+    assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
+                             "VibeGEMM B200 v3"]
+    assert 0 <= vg.default_version() < len(vg.versions())
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions()
 
@@ -72,6 +73,9 @@ def test_plan_aligned_square(vg):
     assert p1["cta_group"] == 1 and p1["grid"] == 148 and p1["num_m_tiles"] == 64
     p0 = vg.plan(0, 8192, 8192, 8192, 256, 256, 256)
     assert p0["persistent"] == 0 and p0["grid"] == 64 * 32 and p0["epilogue"] == "direct_f16"
+    p3 = vg.plan(3, 8192, 8192, 8192, 256, 256, 256)
+    assert (p3["cta_group"], p3["tile_n"], p3["stages"]) == (2, 512, 4)
+    assert (p3["num_m_tiles"], p3["num_n_tiles"]) == (32, 16) and p3["grid"] == 148
 
 
 def test_plan_tails_and_alignment(vg):

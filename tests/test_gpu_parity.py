@@ -4,7 +4,9 @@ GEMM) and with the reference's judge (cuBLAS), through the C ABI.
 Bars (written here, per the reference's validation):
   * fp16 output: the reference's check_error (|r-c| <= 1e-3 + 1e-2*|r|, include/utils.cuh:70-118)
     against the oracle's fp16 result and against cuBLAS, plus at most 1 fp16 ulp of difference
-    from the oracle wherever |C| >= 2^-4 (fp32 accumulation-order noise can flip one rounding);
+    from the oracle wherever |C| >= max(2^-4, K/4096). Accumulation-order noise of an fp32 sum
+    is absolute (~K/3 * 2^-24 for these inputs), so only where one fp16 ulp is well above it can
+    the two roundings differ by at most one step;
   * fp32 validation output: max abs error <= 2e-2*sqrt(K/1024) and max relative error
     |c-r|/max(|r|, that bound) <= 1e-2 against the fp64-accumulated product.
 """
@@ -15,7 +17,7 @@ from conftest import to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
-VERSIONS = [0, 1, 2]
+VERSIONS = [0, 1, 2, 3]
 # (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
 # epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
 SHAPES = [
@@ -41,10 +43,10 @@ def ulp_diff(a_bits, b_bits):
     return np.abs(key(a_bits) - key(b_bits))
 
 
-def check_fp16(orc, got, ref, what):
+def check_fp16(orc, got, ref, what, K):
     ok, st = orc.check_error(ref, got)
     assert ok, (what, st)
-    big = np.abs(ref.view(np.float16).astype(np.float32)) >= 2.0 ** -4
+    big = np.abs(ref.view(np.float16).astype(np.float32)) >= max(2.0 ** -4, K / 4096.0)
     if big.any():
         assert ulp_diff(got[big], ref[big]).max() <= 1, what
 
@@ -68,7 +70,7 @@ def test_fp16_matches_oracle_and_cublas(vg, orc, cases, version, shape):
     Cb = vg.cublas_gemm(dA, dB)
     torch.cuda.synchronize()
     got, cub = to_host(C), to_host(Cb)
-    check_fp16(orc, got, ref16, f"v{version} vs oracle {shape}")
+    check_fp16(orc, got, ref16, f"v{version} vs oracle {shape}", shape[2])
     ok, st = orc.check_error(cub, got)
     assert ok, ("vs cuBLAS", st)
     assert vg.device_status() == 0
@@ -103,7 +105,7 @@ def test_misaligned_operands(vg, orc, version):
     C = bufC[5:5 + M * N].view(M, N)
     vg.gemm(dA, dB, out=C, version=version)
     torch.cuda.synchronize()
-    check_fp16(orc, to_host(C), ref, "misaligned")
+    check_fp16(orc, to_host(C), ref, "misaligned", K)
     # The guard elements around C are untouched.
     assert float(bufC[:5].abs().sum()) == 0.0 and float(bufC[5 + M * N:].abs().sum()) == 0.0
 
@@ -143,7 +145,7 @@ def test_stream_argument(vg, orc):
     with torch.cuda.stream(s):
         C = vg.gemm(dA, dB, stream=s)
     s.synchronize()
-    check_fp16(orc, to_host(C), orc.gemm_f16(A, B), "stream")
+    check_fp16(orc, to_host(C), orc.gemm_f16(A, B), "stream", K)
 
 
 def test_repeated_calls_deterministic(vg, orc):

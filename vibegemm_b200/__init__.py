@@ -33,6 +33,7 @@ _SIGS = {
     "vg_b200_teardown": (None, []),
     "vg_b200_device_status": (ctypes.c_uint, [ctypes.c_int]),
     "vg_b200_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_ulonglong]),
+    "vg_b200_set_raster_group": (ctypes.c_int, [ctypes.c_int]),
     "vg_b200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_ulonglong]),
     "vg_shard_rows": (None, [ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
                              ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong)]),
@@ -50,7 +51,7 @@ _SIGS = {
 EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
-               "num_n_tiles", "num_kb", "group_m", "grid", "persistent")
+               "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n")
 EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32"}
 
 
@@ -172,6 +173,11 @@ def set_wait_timeout_ns(ns: int) -> None:
     lib().vg_b200_set_wait_timeout_ns(ns)
 
 
+def set_raster_group(group_m: int) -> None:
+    """Raster group height (M tiles) for the persistent kernels; 0 = version default."""
+    _check(lib().vg_b200_set_raster_group(group_m), "vg_b200_set_raster_group")
+
+
 def selftest_wait_timeout(timeout_ns: int) -> bool:
     return bool(lib().vg_b200_selftest_wait_timeout(timeout_ns))
 
@@ -190,7 +196,7 @@ def raster_tile(t: int, num_m: int, num_n: int, group_m: int) -> tuple[int, int]
 
 def plan(version: int, M: int, N: int, K: int, a_ptr: int = 0, b_ptr: int = 0, c_ptr: int = 0,
          f32_out: bool = False, num_sms: int = 148) -> dict:
-    out = (ctypes.c_int * 12)()
+    out = (ctypes.c_int * len(PLAN_FIELDS))()
     _check(lib().vg_b200_plan(version, M, N, K, a_ptr, b_ptr, c_ptr, int(f32_out), num_sms, out),
            "vg_b200_plan")
     d = dict(zip(PLAN_FIELDS, list(out)))

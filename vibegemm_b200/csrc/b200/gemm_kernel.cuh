@@ -13,14 +13,21 @@
 //               predicated direct stores (unaligned C / fp32 validation output).
 //
 // CG = 1: one CTA computes a 128×256 tile with tcgen05.mma.cta_group::1 (M=128,N=256).
-// CG = 2: a CTA pair computes a 256×256 tile with tcgen05.mma.cta_group::2 (M=256,
-//         N=256). Each CTA loads its own 128 rows of A and its own 128 rows of B with
-//         ordinary (non-multicast) TMA loads whose completion is counted on the
-//         leader's barrier; the leader issues the MMAs, and tcgen05.commit arrives on
-//         both CTAs' barriers. Each CTA's TMEM holds its 128 rows of the tile.
+// CG = 2: a CTA pair computes a 256×BN tile with tcgen05.mma.cta_group::2 (M=256,
+//         N=256 per instruction). Each CTA loads its own 128 rows of A and its own
+//         BN/2 rows of B with ordinary (non-multicast) TMA loads whose completion is
+//         counted on the leader's barrier; the leader issues the MMAs, and
+//         tcgen05.commit arrives on both CTAs' barriers. Each CTA's TMEM holds its
+//         128 rows of the tile.
 //
-// The accumulator is double-buffered in TMEM, so the epilogue of tile i overlaps the
-// main loop of tile i+1. Tiles are visited persistently with a grouped raster.
+// BN = 256: the 128×256 fp32 accumulator is double-buffered in TMEM (2 × 256
+//           columns), so the epilogue of tile i overlaps the main loop of tile i+1.
+// BN = 512: one 128×512 accumulator fills TMEM; each K step issues two N=256 MMAs
+//           (the "halves"). The epilogue hands each half back as soon as it has read
+//           it, and the next tile runs half 0 ahead over the first STAGES k-blocks
+//           while half 1 is still being drained. Per FLOP this moves 3/4 of the
+//           L2→SMEM bytes of BN = 256 and issues half as many TMA loads.
+// Tiles are visited persistently with a grouped raster.
 //
 // Every mbarrier wait is bounded: after `timeout_ns` without progress the waiting
 // thread records a code in `vg_status_word`, raises a CTA-local abort flag and all
@@ -64,23 +71,37 @@ struct GemmArgs {
     unsigned long long timeout_ns;
 };
 
-template <int CG> struct TileCfg {
+template <int CG, int BN_> struct TileCfg {
+    static_assert(BN_ == 256 || (BN_ == 512 && CG == 2), "tile: 128x256, pair 256x256 or 256x512");
     static constexpr int BM = 128;          // accumulator rows per CTA (TMEM lanes)
-    static constexpr int BN = 256;          // tile columns (fp32 TMEM columns per buffer)
+    static constexpr int BN = BN_;          // tile columns
     static constexpr int BK = 64;           // fp16 per 128-B swizzle row
-    static constexpr int B_ROWS = BN / CG;  // rows of B each CTA loads
+    static constexpr int NSUB = BN / 256;   // N=256 MMAs per K step
+    static constexpr int ACC_BUFS = (NSUB == 1) ? 2 : 1;
+    static constexpr int B_ROWS = BN / CG;  // rows of B each CTA loads (one TMA box, <= 256)
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
+    static constexpr int B_SUB_BYTES = B_BYTES / NSUB; // this CTA's B rows feeding one MMA
     static constexpr int STAGE_TX = CG * (A_BYTES + B_BYTES); // bytes landing per stage
-    static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, BN);
+    static constexpr int TMEM_COLS = 512;
+    static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, 256);
     static constexpr int EPI_WARPS = 4;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int STG_BYTES = 32 * 128; // one 32-row × 64-col fp16 box
 };
 
-template <int CG, int STAGES, int EPI> struct SmemLayout {
-    using T = TileCfg<CG>;
+// Column of C (relative to the tile's first column) held in accumulator column t.
+// With two MMAs per K step, MMA h reads rows [128h, 128h+128) of each CTA's B slab,
+// and CTA q's slab holds C columns [256q, 256q+256) of the tile.
+template <int NSUB> __host__ __device__ __forceinline__ int acc_col_to_c(int t) {
+    if constexpr (NSUB == 1)
+        return t;
+    else
+        return ((t & 255) >> 7 << 8) + ((t >> 8) << 7) + (t & 127);
+}
+
+template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
+    using T = TileCfg<CG, BN>;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
     static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
@@ -99,10 +120,9 @@ __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile i
                                        unsigned long long timeout_ns, unsigned code) {
     const uint64_t t0 = ptx::global_timer_ns();
     while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 128; ++i)
-            if (ptx::mbar_try_wait(bar, parity))
-                return true;
+        // Suspend in hardware (up to ~0.1 ms per probe) rather than spin.
+        if (ptx::mbar_try_wait_sleep(bar, parity, 100000u))
+            return true;
         if (*abort_flag)
             return false;
         if (ptx::global_timer_ns() - t0 > timeout_ns) {
@@ -125,14 +145,14 @@ __device__ __forceinline__ uint32_t pack_half2(uint32_t lo_bits, uint32_t hi_bit
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-template <int CG, int STAGES, int EPI>
-__global__ void __launch_bounds__(TileCfg<CG>::THREADS, 1)
+template <int CG, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-    using T = TileCfg<CG>;
-    using L = SmemLayout<CG, STAGES, EPI>;
+    using T = TileCfg<CG, BN>;
+    using L = SmemLayout<CG, BN, STAGES, EPI>;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = ptx::smem_u32(smem_raw);
@@ -261,47 +281,106 @@ __global__ void __launch_bounds__(TileCfg<CG>::THREADS, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             bool any = false;
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-                if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
-                              kStatusTimeoutMma)) {
-                    ok = false;
-                    break;
+            auto advance = [&]() {
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
-                ptx::tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::BN);
-                for (int kb = 0; kb < args.num_kb; ++kb) {
-                    if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+            };
+            // MMAs of one k-block for accumulator half `h` (columns [256h, 256h+256)).
+            auto issue = [&](uint32_t d, int h, int kb) {
+                const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
+                const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES + h * T::B_SUB_BYTES);
+#pragma unroll
+                for (int k = 0; k < T::BK / 16; ++k) {
+                    // +32 B per 16-element K step = +2 in the start-address field.
+                    ptx::mma_f16<CG>(d + 256u * h, a0 + 2u * k, b0 + 2u * k, T::IDESC,
+                                     (kb | k) != 0 ? 1u : 0u);
+                }
+            };
+            auto commit_to = [&](uint32_t bar) {
+                if constexpr (CG == 1)
+                    ptx::mma_commit(bar);
+                else
+                    ptx::mma_commit_pair(bar, 0x3);
+            };
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+                if constexpr (T::ACC_BUFS == 2) {
+                    if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
+                                  kStatusTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
-                    const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
-                    const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES);
-#pragma unroll
-                    for (int k = 0; k < T::BK / 16; ++k) {
-                        // +32 B per 16-element K step = +2 in the start-address field.
-                        ptx::mma_f16<CG>(d, a0 + 2u * k, b0 + 2u * k, T::IDESC,
-                                         (kb | k) != 0 ? 1u : 0u);
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::BN);
+                    for (int kb = 0; kb < args.num_kb; ++kb) {
+                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        issue(d, 0, kb);
+                        any = true;
+                        commit_to(empty_bar(stage));
+                        advance();
                     }
-                    any = true;
-                    if constexpr (CG == 1)
-                        ptx::mma_commit(empty_bar(stage));
-                    else
-                        ptx::mma_commit_pair(empty_bar(stage), 0x3);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
+                    if (!ok)
+                        break;
+                    commit_to(tfull_bar(acc));
+                    acc ^= 1;
+                    if (acc == 0)
+                        acc_phase ^= 1u;
+                } else {
+                    // Half 0 runs ahead over the first `run` k-blocks while the epilogue
+                    // still drains half 1 of the previous tile.
+                    if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
                     }
-                }
-                if (!ok)
-                    break;
-                if constexpr (CG == 1)
-                    ptx::mma_commit(tfull_bar(acc));
-                else
-                    ptx::mma_commit_pair(tfull_bar(acc), 0x3);
-                acc ^= 1;
-                if (acc == 0)
+                    ptx::tc_fence_after();
+                    const int run = args.num_kb < STAGES ? args.num_kb : STAGES;
+                    const int s0 = stage;
+                    const uint32_t p0 = phase;
+                    for (int kb = 0; kb < run; ++kb) {
+                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        issue(tmem_base, 0, kb);
+                        any = true;
+                        advance();
+                    }
+                    if (!ok)
+                        break;
+                    if (!wait_bar(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    stage = s0;
+                    phase = p0;
+                    for (int kb = 0; kb < run; ++kb) {
+                        issue(tmem_base, 1, kb);
+                        commit_to(empty_bar(stage));
+                        advance();
+                    }
+                    for (int kb = run; kb < args.num_kb; ++kb) {
+                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        issue(tmem_base, 0, kb);
+                        issue(tmem_base, 1, kb);
+                        commit_to(empty_bar(stage));
+                        advance();
+                    }
+                    if (!ok)
+                        break;
+                    commit_to(tfull_bar(0));
                     acc_phase ^= 1u;
+                }
             }
             // Every MMA issued by this thread must complete before TMEM is freed.
             if (any) {
@@ -336,25 +415,27 @@ __global__ void __launch_bounds__(TileCfg<CG>::THREADS, 1)
             const int row0 = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
             const int col0 = tn * T::BN;
             const uint32_t t_row =
-                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::BN);
+                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * 256);
 #pragma unroll 1
             for (int c = 0; c < T::BN / 64; ++c) {
                 uint32_t v0[32], v1[32];
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
                 ptx::tmem_wait_ld();
-                if (c == T::BN / 64 - 1) {
-                    // Accumulator buffer fully read: hand it back to the MMA issuer.
+                // Last read of a release unit (a whole buffer, or one half of the BN=512
+                // accumulator): hand those TMEM columns back to the MMA issuer.
+                if (c % 4 == 3) {
+                    const int unit = (T::ACC_BUFS == 2) ? acc : (c >> 2);
                     ptx::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
                         if constexpr (CG == 1)
-                            ptx::mbar_arrive(tempty_bar(acc));
+                            ptx::mbar_arrive(tempty_bar(unit));
                         else
-                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(acc), 0));
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
                     }
                 }
-                const int ccol = col0 + c * 64;
+                const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
                 if constexpr (EPI == kEpiTmaF16) {
                     uint32_t p[32];
 #pragma unroll
@@ -431,9 +512,13 @@ __global__ void __launch_bounds__(TileCfg<CG>::THREADS, 1)
                     }
                 }
             }
-            acc ^= 1;
-            if (acc == 0)
+            if constexpr (T::ACC_BUFS == 2) {
+                acc ^= 1;
+                if (acc == 0)
+                    acc_phase ^= 1u;
+            } else {
                 acc_phase ^= 1u;
+            }
         }
         if constexpr (EPI == kEpiTmaF16) {
             if (lane == 0)

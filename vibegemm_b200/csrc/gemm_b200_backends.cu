@@ -37,6 +37,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v2 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<2>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v2
+namespace gemm_b200_v3 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<3>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v3
 
 using KernelFn = void (*)(half *, half *, half *, int, int, int);
 
@@ -64,3 +67,4 @@ template <KernelFn Fn> class GeneratedB200KernelBackend : public GemmBackend {
 REGISTER_B200_KERNEL("VibeGEMM B200 v0", GeneratedB200KernelBackend<gemm_b200_v0::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v1", GeneratedB200KernelBackend<gemm_b200_v1::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v2", GeneratedB200KernelBackend<gemm_b200_v2::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v3", GeneratedB200KernelBackend<gemm_b200_v3::launchKernel>);

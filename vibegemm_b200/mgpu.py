@@ -1,0 +1,64 @@
+"""Row-block sharding of one GEMM across the GPUs of a node (one process per GPU).
+
+C[M,N] = A[M,K] · B[N,K]^T is split by contiguous row blocks of A (and C): rank r owns
+rows [r·ceil(M/P), min(M, (r+1)·ceil(M/P))) — the same split as the C ABI's
+``vg_shard_rows``. B is replicated on every rank. K is never split, so the data path
+needs no reduction; the only optional collective is an all-gather of C, which is
+copy-free because the row-major C shards are contiguous slices of the full C
+(uneven last shards are padded to the common block height for the collective).
+
+The compute step is a parameter (``gemm_fn``): the B200 kernel on GPUs, the CPU oracle in
+the world-size-2 gloo tests of this host logic.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+
+def shard_rows(M: int, world: int, rank: int) -> tuple[int, int]:
+    """(row0, rows) of rank `rank`; identical to vg_shard_rows in the C ABI."""
+    if M <= 0 or world <= 0 or not 0 <= rank < world:
+        return 0, 0
+    per = -(-M // world)
+    lo = min(M, per * rank)
+    hi = min(M, lo + per)
+    return lo, hi - lo
+
+
+@dataclass
+class RowShardedGemm:
+    M: int
+    N: int
+    K: int
+    rank: int
+    world: int
+
+    @property
+    def block_rows(self) -> int:
+        return -(-self.M // self.world) if self.M > 0 else 0
+
+    @property
+    def local(self) -> tuple[int, int]:
+        return shard_rows(self.M, self.world, self.rank)
+
+    def run(self, A_local, B, C_local, gemm_fn: Callable) -> None:
+        """Local shard product: C_local[rows, N] = A_local[rows, K] · B^T."""
+        if self.local[1] > 0:
+            gemm_fn(A_local, B, C_local)
+
+    def gather(self, C_local, group=None):
+        """All-gather of the row shards into the full M×N C (returned on every rank)."""
+        import torch
+        import torch.distributed as dist
+
+        rows = self.local[1]
+        blk = self.block_rows
+        send = C_local
+        if rows != blk:  # uneven tail shard: pad to the common block height
+            send = torch.zeros((blk, self.N), dtype=C_local.dtype, device=C_local.device)
+            if rows:
+                send[:rows].copy_(C_local[:rows])
+        full = torch.empty((blk * self.world, self.N), dtype=C_local.dtype, device=C_local.device)
+        dist.all_gather_into_tensor(full, send.contiguous(), group=group)
+        return full[: self.M]
