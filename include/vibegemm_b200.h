@@ -40,6 +40,29 @@ int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
 int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C, int M, int N,
                              int K, vg_stream_t stream);
 
+/* Allocation-free form of vg_b200_gemm_f16 (no counterpart in the reference).
+ *
+ * For callers that must not allocate device memory: programs that hand the whole GPU to
+ * their own memory pool and forbid side allocations, latency-critical loops where an
+ * allocation could stall or fail under memory pressure, and hosts with a device-memory
+ * budget fixed at start-up. vg_b200_gemm_f16 takes the buffer for its K-padding pre-pass
+ * (needed when K % 8 != 0 or A/B is not 16-byte aligned) from the CUDA stream-ordered
+ * pool; this entry point uses a fixed 32 MiB array in the library's device memory
+ * instead and never calls cudaMalloc, cudaMallocAsync, cudaFree or an allocating library.
+ *   - Limit: the padded copies (M + N) * roundup(K, 8) * 2 bytes must fit in 32 MiB;
+ *     larger padded problems return VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing.
+ *     Problems that need no padding have no size limit.
+ *   - The 32 MiB are held on every GPU that loads the library until the process exits.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls share the array: calls that overlap on the GPU (different streams, or
+ *     different host threads on one device) race on it; serialise them. Each call
+ *     rewrites every scratch byte it reads, so no clearing is needed between calls.
+ * Same semantics, arguments and return codes as vg_b200_gemm_f16 otherwise. */
+#define VG_ERROR_NOALLOC_SCRATCH_LIMIT 2001
+int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
+                             vg_stream_t stream);
+
 /* Validation build: the same main loop as `version`, fp32 C (no fp16 rounding), so
  * accumulation error can be judged separately from output quantisation. No
  * counterpart in the reference (its only check is fp16-vs-cuBLAS,

@@ -25,6 +25,7 @@ _SIGS = {
     "vg_b200_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_b200_gemm_f16_version": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_b200_gemm_f16_f32out": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_b200_gemm_f16_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_cublas_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_b200_num_versions": (ctypes.c_int, []),
     "vg_b200_version_name": (ctypes.c_char_p, [ctypes.c_int]),
@@ -124,6 +125,22 @@ def gemm(A, B, out=None, version: Optional[int] = None, stream=None):
         code = lib().vg_b200_gemm_f16_version(version, A.data_ptr(), B.data_ptr(), out.data_ptr(),
                                               M, N, K, s)
     _check(code, "vg_b200_gemm_f16")
+    return out
+
+
+NOALLOC_SCRATCH_LIMIT = 2001  # VG_ERROR_NOALLOC_SCRATCH_LIMIT
+
+
+def gemm_noalloc(A, B, out=None, stream=None):
+    """vg_b200_gemm_f16 without any device allocation: the K-padding workspace is a fixed
+    32 MiB array in the library (problems whose padded copies exceed it raise
+    VibeGemmError with code NOALLOC_SCRATCH_LIMIT). Overlapping calls on one GPU race on
+    that array; the caller must allocate `out` itself to avoid torch's allocator."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float16)
+    code = lib().vg_b200_gemm_f16_noalloc(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K,
+                                          _stream_handle(stream))
+    _check(code, "vg_b200_gemm_f16_noalloc")
     return out
 
 

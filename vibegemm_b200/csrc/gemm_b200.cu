@@ -475,6 +475,125 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     return e;
 }
 
+// ── allocation-free variant ─────────────────────────────────────────────────
+// Pad workspace of vg_b200_gemm_f16_noalloc: a fixed array in the module's device
+// memory instead of the stream-ordered pool. Every GPU that loads this library holds
+// these kNoAllocScratchBytes until the process exits. In host code the name
+// `noalloc_scratch` is only a host-side stand-in for the symbol; its device address
+// comes from cudaGetSymbolAddress, taken once per device with that device current.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
+static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
+
+struct ScratchAddr {
+    void *ptr = nullptr;
+    cudaError_t err = cudaSuccess;
+};
+ScratchAddr g_scratch[kMaxDevices];
+std::once_flag g_scratch_once[kMaxDevices];
+
+const ScratchAddr &noalloc_scratch_addr(int dev) {
+    std::call_once(g_scratch_once[dev], [dev] {
+        ScratchAddr &s = g_scratch[dev];
+        s.err = cudaGetSymbolAddress(&s.ptr, noalloc_scratch);
+        if (s.err != cudaSuccess) {
+            s.ptr = nullptr;
+            (void)cudaGetLastError();
+        }
+    });
+    return g_scratch[dev];
+}
+
+inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Same plan, descriptors and launches as run_gemm for the default version, with the
+// K-padding workspace taken from noalloc_scratch; nothing is allocated or freed.
+// Returns a cudaError_t value or VG_ERROR_NOALLOC_SCRATCH_LIMIT.
+int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K, cudaStream_t s) {
+    const int version = kDefaultVersion;
+    if (M < 0 || N < 0 || K < 0)
+        return cudaErrorInvalidValue;
+    if (M == 0 || N == 0)
+        return cudaSuccess;
+    if (!C)
+        return cudaErrorInvalidValue;
+    if (K == 0)
+        return cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), s);
+    if (!A || !B)
+        return cudaErrorInvalidValue;
+
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    const DeviceInfo *di = device_info(dev);
+    if (!di || !di->ok)
+        return cudaErrorInvalidDevice;
+    if (di->major != 10 || di->minor != 0)
+        return cudaErrorNoKernelImageForDevice;
+
+    Plan p;
+    e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, false,
+                               di->num_sms, di->num_sms / 2, p);
+    if (e != cudaSuccess)
+        return e;
+    const int Kp = p.Kp;
+    const size_t a_bytes = p.pad_a ? round_up_256((size_t)M * Kp * sizeof(__half)) : 0;
+    const size_t b_bytes = p.pad_b ? (size_t)N * Kp * sizeof(__half) : 0;
+    if (a_bytes + b_bytes > kNoAllocScratchBytes)
+        return VG_ERROR_NOALLOC_SCRATCH_LIMIT;
+
+    int max_clusters = 0;
+    e = dispatch(p, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
+    if (e != cudaSuccess)
+        return e;
+    int grid = p.grid;
+    if (p.cta_group == 2 && p.persistent && max_clusters > 0)
+        grid = std::min(grid, 2 * max_clusters);
+
+    const void *A_use = A, *B_use = B;
+    if (p.pad_a || p.pad_b) {
+        const ScratchAddr &sc = noalloc_scratch_addr(dev);
+        if (sc.err != cudaSuccess)
+            return sc.err;
+        __half *wa = static_cast<__half *>(sc.ptr);
+        __half *wb = reinterpret_cast<__half *>(static_cast<char *>(sc.ptr) + a_bytes);
+        if (p.pad_a) {
+            e = launch_pad(A, M, K, wa, Kp, di->num_sms, s);
+            A_use = wa;
+        }
+        if (e == cudaSuccess && p.pad_b) {
+            e = launch_pad(B, N, K, wb, Kp, di->num_sms, s);
+            B_use = wb;
+        }
+        if (e != cudaSuccess)
+            return e;
+    }
+
+    CUtensorMap ma, mb, mc;
+    std::memset(&mc, 0, sizeof(mc));
+    const uint32_t b_box_rows = (uint32_t)(p.bn / p.cta_group);
+    bool ok = get_map(ma, A_use, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp, 64u, 128u, dev) &&
+              get_map(mb, B_use, (uint64_t)Kp, (uint64_t)N, (uint64_t)Kp, 64u, b_box_rows, dev);
+    if (ok && p.epi == kEpiTmaF16)
+        ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
+    if (!ok)
+        return cudaErrorInvalidValue;
+
+    GemmArgs args{};
+    args.M = M;
+    args.N = N;
+    args.K = Kp;
+    args.num_m_tiles = p.num_m_tiles;
+    args.num_n_tiles = p.num_n_tiles;
+    args.num_kb = p.num_kb;
+    args.group_m = p.group_m;
+    args.c_vec_ok = (N % 8 == 0) && aligned16((uintptr_t)C);
+    args.C = C;
+    args.ldc = N;
+    args.timeout_ns = wait_timeout_ns();
+    return dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+}
+
 } // namespace
 } // namespace vg
 
@@ -494,6 +613,11 @@ int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
 int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C, int M, int N,
                             int K, vg_stream_t stream) {
     return (int)vg::run_gemm(version, A, B, C, M, N, K, true, (cudaStream_t)stream);
+}
+
+int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
+                             vg_stream_t stream) {
+    return vg::run_gemm_noalloc(A, B, C, M, N, K, (cudaStream_t)stream);
 }
 
 int vg_b200_num_versions(void) { return vg::kNumVersions; }
