@@ -27,14 +27,15 @@ extern "C" {
 
 typedef struct CUstream_st *vg_stream_t;
 
-/* Default B200 kernel (the fastest registered version).
+/* Default B200 kernel: the version chosen per shape ("VibeGEMM B200 auto", version -1).
  * Replaces GemmBackend::run (include/backend.cuh:13) of a registered backend and the
  * per-version free function launchKernel(half*,half*,half*,int,int,int)
  * (csrc/h100/gemm_8192x8192_v18.cuh:545, bound through csrc/gemm_h100_backends.cu:41). */
 int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
                      vg_stream_t stream);
 
-/* One specific kernel version of the B200 ladder, 0 <= version < vg_b200_num_versions().
+/* One specific kernel version of the B200 ladder, 0 <= version < vg_b200_num_versions(),
+ * or -1 for the per-shape choice of vg_b200_gemm_f16.
  * Replaces gemm_8192x8192_vN::launchKernel (csrc/h100/gemm_8192x8192_v*.cuh), one per
  * registered "VibeGEMM B200 vN" backend (registry.cuh:68-70 pattern). */
 int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C, int M, int N,
@@ -77,7 +78,8 @@ int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int 
                        vg_stream_t stream);
 
 /* Registry listing: replaces KernelRegistry::make_all / GemmBackend::name
- * (include/registry.cuh:23-32, include/backend.cuh:16). */
+ * (include/registry.cuh:23-32, include/backend.cuh:16). vg_b200_default_version() is -1
+ * (per-shape choice); vg_b200_version_name(-1) is "VibeGEMM B200 auto". */
 int vg_b200_num_versions(void);
 const char *vg_b200_version_name(int version);
 int vg_b200_default_version(void);
@@ -117,9 +119,10 @@ void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *
 
 /* Host-side launch plan for a problem, as the launcher would build it for a device
  * with `num_sms` SMs (exposed so the planner can be tested without a GPU).
- * Fields of `out` (int[13]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct
- * fp16, 2 direct fp32), pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb,
- * group_m, grid (CTAs), persistent, tile columns. Returns 0 or a cudaError_t code. */
+ * `version` may be -1 (per-shape choice). Fields of `out` (int[14]): cta_group, stages,
+ * epilogue kind (0 TMA fp16, 1 direct fp16, 2 direct fp32), pad_a, pad_b, padded K,
+ * num_m_tiles, num_n_tiles, num_kb, group_m, grid (CTAs), persistent, tile columns,
+ * resolved version. Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int f32_out, int num_sms, int *out);
 

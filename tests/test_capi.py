@@ -29,9 +29,9 @@ def test_library_exports_every_declared_symbol(vg):
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3"]
-    assert 0 <= vg.default_version() < len(vg.versions())
+    assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
-    assert vg.backends() == ["cuBLAS"] + vg.versions()
+    assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
 
 
 @pytest.mark.parametrize("num_m,num_n,group", [(1, 1, 8), (32, 32, 8), (7, 13, 8), (33, 5, 4),
@@ -76,6 +76,18 @@ def test_plan_aligned_square(vg):
     p3 = vg.plan(3, 8192, 8192, 8192, 256, 256, 256)
     assert (p3["cta_group"], p3["tile_n"], p3["stages"]) == (2, 512, 4)
     assert (p3["num_m_tiles"], p3["num_n_tiles"]) == (32, 16) and p3["grid"] == 148
+
+
+@pytest.mark.parametrize("shape,want", [
+    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 3), ((4096, 14336, 4096), 3),
+    ((4096, 4096, 14336), 3), ((8191, 8193, 4099), 3),
+    ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
+    ((1000, 3000, 2048), 1),     # fewer pair tiles than pair slots: single-CTA tiles
+    ((512, 512, 512), 1),
+])
+def test_auto_version_choice(vg, shape, want):
+    assert vg.plan(-1, *shape, 256, 256, 256)["version"] == want
+    assert vg.plan(want, *shape, 256, 256, 256)["version"] == want
 
 
 def test_plan_tails_and_alignment(vg):

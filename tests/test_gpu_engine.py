@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 def test_engine_passes_every_backend_512(vg):
     res = vg.engine_execute(512, 512, 512)
     names = [r["name"] for r in res]
-    assert names == ["cuBLAS"] + vg.versions()
+    assert names == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
     for r in res:
         assert not r["skipped"], r
         assert r["passed"], r

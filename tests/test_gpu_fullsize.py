@@ -1,0 +1,56 @@
+"""Full-size parity at the BASELINE configurations.
+
+The judge here is the reference's own naive kernel (csrc/a100/gemm_8192x8192_v0.cuh,
+compiled for sm_100a into oracle/_ref by `make -C oracle ref`): sequential-k fp32
+accumulation, i.e. exactly the semantics of the CPU oracle (bit-identical to it, checked
+below on sampled rows), but fast enough on the GPU to compare every element of an
+8192³ product. Criterion: the reference's check_error (atol 1e-3, rtol 1e-2) over every
+element, plus the CPU oracle on sampled first/last rows. Skipped where oracle/_ref was not
+built (the reference tree is needed at build time).
+
+cuBLAS is not the judge at odd K: with lda = 4099 it fails the reference's check_error
+against the oracle (measured on a B200 with cuBLAS 12.9), while every kernel here passes.
+"""
+import numpy as np
+import pytest
+
+from conftest import to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = [
+    (8192, 8192, 8192, "uniform"),   # headline
+    (8191, 8193, 4099, "uniform"),   # tails, unaligned K and N (pad pre-pass, direct epilogue)
+    (1000, 3000, 2048, "uniform"),   # partial tiles, under-filled grid
+    (4096, 14336, 4096, "normal"),   # LLM projection
+    (4096, 4096, 14336, "normal"),   # long K
+    (8192, 8192, 512, "normal"),     # short K
+]
+
+
+@pytest.fixture(scope="module")
+def ref_gpu(orc):
+    G = orc.ref_gpu()
+    if G is None:
+        pytest.skip("oracle/_ref/libvgref_gpu.so not built")
+    return G
+
+
+@pytest.mark.parametrize("cfg", CONFIGS, ids=lambda c: "x".join(map(str, c[:3])) + "_" + c[3])
+def test_fullsize_vs_reference_naive_kernel(vg, orc, ref_gpu, cfg):
+    import torch
+    M, N, K, dist = cfg
+    A, B = orc.make_inputs(M, N, K, dist)
+    dA, dB = to_dev(A), to_dev(B)
+    naive = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+    assert ref_gpu.vgref_naive_gemm(dA.data_ptr(), dB.data_ptr(), naive.data_ptr(), M, N, K) == 0
+    ref = to_host(naive)
+    rows = list(range(4)) + list(range(M - 4, M))
+    # The reference's naive kernel is the oracle's semantics, bit for bit.
+    assert np.array_equal(np.concatenate([orc.gemm_f16(A, B, r, 1) for r in rows]), ref[rows])
+    for v in list(range(len(vg.versions()))) + [-1]:
+        C = vg.gemm(dA, dB, version=v)
+        torch.cuda.synchronize()
+        ok, st = orc.check_error(ref, to_host(C))
+        assert ok, (v, cfg, st)
+    assert vg.device_status() == 0

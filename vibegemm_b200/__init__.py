@@ -52,7 +52,7 @@ _SIGS = {
 EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
-               "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n")
+               "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version")
 EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32"}
 
 
@@ -165,12 +165,23 @@ def cublas_gemm(A, B, out=None, stream=None):
     return out
 
 
+AUTO = -1  # per-shape version choice (the default entry point's policy)
+
+
 def versions() -> list[str]:
     L = lib()
     return [L.vg_b200_version_name(i).decode() for i in range(L.vg_b200_num_versions())]
 
 
+def version_name(version: int) -> str:
+    n = lib().vg_b200_version_name(version)
+    if n is None:
+        raise ValueError(f"no kernel version {version}")
+    return n.decode()
+
+
 def default_version() -> int:
+    """-1: the default entry point chooses a version per shape."""
     return int(lib().vg_b200_default_version())
 
 

@@ -11,8 +11,9 @@
 //       clusters, grouped raster, TMEM double buffer, TMA-store epilogue.
 //   v3  CTA pair, 256×512 tile (one 128×512 fp32 accumulator per CTA = all of TMEM),
 //       4-stage ring of 48 KB, per-half TMEM hand-back with half-0 run-ahead: 3/4 of
-//       v2's L2→SMEM bytes and half its TMA loads per FLOP. Default: under the 1 kW
-//       power cap the lower data movement keeps the SM clock ~15 % higher than v2's.
+//       v2's L2→SMEM bytes and half its TMA loads per FLOP. Under the 1 kW power cap
+//       the lower data movement keeps the SM clock ~15 % higher than v2's.
+//   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
 // strides: when A or B (K % 8 != 0 or a misaligned pointer) cannot be described,
@@ -54,7 +55,23 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v3", 2, 512, 4, true, true, 16},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
-constexpr int kDefaultVersion = 3;
+constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
+
+// Per-shape choice among the ladder, from the measured sweep over the BASELINE shapes:
+// the 256×512 pair tile (v3) wins whenever K is not short and there is at least one
+// full wave of pair tiles; short K (< 1024) favours the double-buffered 256×256 pair
+// (v2), whose epilogue fully overlaps the next tile; grids too small to fill the
+// pairs favour 128×256 single-CTA tiles (v1), which occupy twice as many SMs.
+int select_version(int M, int N, int K, int num_sms) {
+    const long long pairs = num_sms / 2;
+    const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
+    const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
+    if (K >= 1024 && t3 >= pairs)
+        return 3;
+    if (t2 >= pairs)
+        return 2;
+    return 1;
+}
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
 
@@ -74,6 +91,7 @@ int raster_group_override() {
 }
 
 struct Plan {
+    int version = 0; // resolved version (never kAutoVersion)
     int cta_group = 1;
     int bn = 256;
     int stages = 4;
@@ -91,10 +109,15 @@ inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
 // Pure host planning (no CUDA calls): what the launcher will do for this problem.
 int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C, bool f32_out,
               int num_sms, int max_clusters, Plan &p) {
-    if (version < 0 || version >= kNumVersions || M < 0 || N < 0 || K < 0 || num_sms <= 0)
+    if (M < 0 || N < 0 || K < 0 || num_sms <= 0)
+        return cudaErrorInvalidValue;
+    if (version == kAutoVersion)
+        version = select_version(M, N, K, num_sms);
+    if (version < 0 || version >= kNumVersions)
         return cudaErrorInvalidValue;
     const VersionDesc &v = kVersions[version];
     p = Plan{};
+    p.version = version;
     p.cta_group = v.cta_group;
     p.bn = v.bn;
     p.stages = v.stages;
@@ -377,7 +400,7 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
 
 cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
                      bool f32_out, cudaStream_t s) {
-    if (version < 0 || version >= kNumVersions || M < 0 || N < 0 || K < 0)
+    if ((version != kAutoVersion && (version < 0 || version >= kNumVersions)) || M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
         return cudaSuccess;
@@ -509,7 +532,7 @@ inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
 // K-padding workspace taken from noalloc_scratch; nothing is allocated or freed.
 // Returns a cudaError_t value or VG_ERROR_NOALLOC_SCRATCH_LIMIT.
 int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K, cudaStream_t s) {
-    const int version = kDefaultVersion;
+    const int version = kAutoVersion;
     if (M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
@@ -607,7 +630,7 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
 
 int vg_b200_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
                      vg_stream_t stream) {
-    return (int)vg::run_gemm(vg::kDefaultVersion, A, B, C, M, N, K, false, (cudaStream_t)stream);
+    return (int)vg::run_gemm(vg::kAutoVersion, A, B, C, M, N, K, false, (cudaStream_t)stream);
 }
 
 int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C, int M, int N,
@@ -623,12 +646,14 @@ int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N
 int vg_b200_num_versions(void) { return vg::kNumVersions; }
 
 const char *vg_b200_version_name(int version) {
+    if (version == vg::kAutoVersion)
+        return "VibeGEMM B200 auto";
     if (version < 0 || version >= vg::kNumVersions)
         return nullptr;
     return vg::kVersions[version].name;
 }
 
-int vg_b200_default_version(void) { return vg::kDefaultVersion; }
+int vg_b200_default_version(void) { return vg::kAutoVersion; }
 
 int vg_b200_is_available(int device) {
     const vg::DeviceInfo *di = vg::device_info(device);
@@ -731,9 +756,9 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
     const int e = vg::make_plan(version, M, N, K, A, B, C, f32_out != 0, num_sms, num_sms / 2, p);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[13] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
+    const int vals[14] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
                           p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
-                          p.grid,      p.persistent,  p.bn};
+                          p.grid,      p.persistent,  p.bn,          p.version};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }

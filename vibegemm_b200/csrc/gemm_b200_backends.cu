@@ -22,7 +22,7 @@ namespace {
 template <int V> void launch_version(half *A, half *B, half *C, int M, int N, int K) {
     const int e = vg_b200_gemm_f16_version(V, A, B, C, M, N, K, nullptr);
     if (e != 0)
-        std::fprintf(stderr, "VibeGEMM B200 v%d: launch failed: %s\n", V,
+        std::fprintf(stderr, "%s: launch failed: %s\n", vg_b200_version_name(V),
                      cudaGetErrorString((cudaError_t)e));
 }
 
@@ -40,6 +40,10 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v3 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<3>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v3
+// The default entry point: one of the versions above, chosen per shape.
+namespace gemm_b200_auto {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
+} // namespace gemm_b200_auto
 
 using KernelFn = void (*)(half *, half *, half *, int, int, int);
 
@@ -68,3 +72,4 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v0", GeneratedB200KernelBackend<gemm_b200_v0
 REGISTER_B200_KERNEL("VibeGEMM B200 v1", GeneratedB200KernelBackend<gemm_b200_v1::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v2", GeneratedB200KernelBackend<gemm_b200_v2::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v3", GeneratedB200KernelBackend<gemm_b200_v3::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
