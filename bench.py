@@ -4,9 +4,14 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 A step is one C = A·B^T GEMM (fp16 in, fp32 accumulate, fp16 out) of the workload:
-M=N=K=8192 per GPU (the reference's 8192³ headline). With N GPUs (torchrun, one process
-per GPU) A and C are split into contiguous row blocks of 8192 rows per rank and B is
-replicated (weak scaling, no collective in the data path). Rank 0 prints ONE JSON line.
+
+* ``--workload gemm8192`` (default): M=N=K=8192 per GPU (the reference's 8192³ headline).
+  With N GPUs (torchrun, one process per GPU) A and C are split into contiguous row blocks
+  of 8192 rows per rank and B is replicated (weak scaling, no collective in the data path).
+* ``--workload sharded32k``: one M=N=K=32768 GEMM split into N contiguous row blocks of A
+  and C, B replicated (strong scaling; ``--allgather`` also times the NCCL all-gather of C).
+
+Rank 0 prints ONE JSON line.
 
 * ``value``      whole-job TFLOP/s, inputs resident in HBM, CUDA events on the launching
                  stream around exactly K launches, barrier + synchronize on both sides,
@@ -40,7 +45,12 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "FP16 GEMM TFLOP/s @ M=N=K=8192 per B200; % of dense peak; vs cuBLAS"
 UNIT = "TFLOP/s"
-ROWS_PER_GPU, N_DIM, K_DIM = 8192, 8192, 8192
+WORKLOADS = {
+    # name: (rows per GPU or None for a fixed total, total M if fixed, N, K, scaling)
+    "gemm8192": (8192, None, 8192, 8192, "weak"),
+    "sharded32k": (None, 32768, 32768, 32768, "strong"),
+}
+ROWS_PER_GPU, N_DIM, K_DIM = 8192, 8192, 8192  # the default workload (CPU baseline sample)
 FALLBACK_PEAK_TFLOPS = 1590.0  # used only when MEASURED_PEAKS.json is absent
 PROFILE_SUMMARY = ROOT / "profiles" / "gemm_b200_v3_8192.md"
 
@@ -55,6 +65,7 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of C (N>1)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm8192")
     return ap.parse_args()
 
 
@@ -147,8 +158,8 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(mhz)}
 
 
-def cpu_baseline(seconds: float) -> dict:
-    """The oracle GEMM (all host threads) on a bounded row sample of the 8192³ problem."""
+def cpu_baseline(seconds: float, N_DIM: int = N_DIM, K_DIM: int = K_DIM) -> dict:
+    """The oracle GEMM (all host threads) on a bounded row sample of the workload."""
     import numpy as np
     import oracle
 
@@ -165,7 +176,7 @@ def cpu_baseline(seconds: float) -> dict:
     flops = 2.0 * rows * N_DIM * K_DIM
     del np
     return {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{rows} of 8192 rows of the 8192x8192x8192 GEMM ({flops:.3g} FLOP, {dt:.2f} s)"}
+            "sample": f"{rows} rows of the {N_DIM}-column, K={K_DIM} GEMM ({flops:.3g} FLOP, {dt:.2f} s)"}
 
 
 def run_reference(args) -> None:
@@ -229,7 +240,8 @@ def run_b200(args) -> None:
 
     assert vg.is_available(local), "not an sm_100 B200 device"
     version = args.version  # None: the default entry point (per-shape choice)
-    M = ROWS_PER_GPU * world
+    per_gpu, fixed_m, N_DIM, K_DIM, scaling = WORKLOADS[args.workload]
+    M = per_gpu * world if per_gpu else fixed_m
     sh = RowShardedGemm(M, N_DIM, K_DIM, rank, world)
     r0, rows = sh.local
     gen = torch.Generator(device="cuda")
@@ -301,7 +313,7 @@ def run_b200(args) -> None:
         vg.gemm(A, B, out=C, version=version, stream=stream)
         hC.copy_(C, non_blocking=True)
 
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e2e_steps = max(1, min(args.steps, args.e2e_steps if args.workload == "gemm8192" else 2))
     ms_e2e = max_over_ranks(timed(e2e_step, e2e_steps, 3))
     e2e = {"value": flop_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": world * (A.numel() + B.numel()) * 2,
@@ -313,30 +325,34 @@ def run_b200(args) -> None:
         def gather_step():
             sh.gather(C)
         ms_ag = max_over_ranks(timed(gather_step, min(args.steps, 20), 3))
-        allgather = {"ms_per_step": ms_ag, "bytes_per_rank": M * N_DIM * 2}
+        allgather = {"ms_per_step": ms_ag, "bytes_gathered": M * N_DIM * 2,
+                     "gemm_plus_allgather_value": flop_step / ((ms + ms_ag) * 1e-3) / 1e12,
+                     "note": "NCCL all_gather_into_tensor of the row-major C shards, timed after the GEMM"}
 
     pk = peaks()
     per_gpu_launch_tflops = 2.0 * rows * N_DIM * K_DIM / (ms_local * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": per_gpu_launch_tflops, "peak": pk["tflops"], "unit": UNIT,
             "frac": per_gpu_launch_tflops / pk["tflops"], "traffic": profile_traffic(),
             "peak_source": pk["source"],
-            "algorithmic": "2*M*N*K FLOP per launch (M=8192 rows of this GPU, N=K=8192)"}
+            "algorithmic": f"2*M*N*K FLOP per launch (M={rows} rows of this GPU, N={N_DIM}, K={K_DIM})"}
 
     cpu = None
     if rank == 0 and world == 1:
-        cpu = cpu_baseline(args.cpu_seconds)
+        cpu = cpu_baseline(args.cpu_seconds, N_DIM, K_DIM)
 
     clocks = sampler.summary()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f16", "accumulate": "f32", "data": "synthetic",
-            "config": {"workload": "fp16_gemm_8192x8192x8192_per_gpu", "M": M, "N": N_DIM, "K": K_DIM,
-                       "rows_per_gpu": ROWS_PER_GPU, "parallelism": f"row-block x{world} (B replicated)",
+            "config": {"workload": ("fp16_gemm_8192x8192x8192_per_gpu" if args.workload == "gemm8192"
+                                    else "fp16_gemm_32768x32768x32768_row_sharded"),
+                       "M": M, "N": N_DIM, "K": K_DIM,
+                       "rows_per_gpu": rows, "parallelism": f"row-block x{world} (B replicated)",
                        "layout": "A MxK row-major, B NxK (K contiguous), C MxN row-major",
                        "inputs": "uniform[-1,1] fp16, seeded device generator",
-                       "l2": "inputs larger than L2 (384 MiB per GPU per step vs 126 MB L2)",
+                       "l2": f"inputs larger than L2 ({(rows * K_DIM + N_DIM * K_DIM + rows * N_DIM) * 2 >> 20} MiB per GPU per step vs 126 MB L2)",
                        "kernel": vg.version_name(plan["version"]) + (" (via vg_b200_gemm_f16, per-shape choice)" if version is None else "")},
             "pct_of_peak": per_gpu_launch_tflops / pk["tflops"],
             "cublas": {"value": flop_step / (ms_cublas * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms_cublas,
