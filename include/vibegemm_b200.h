@@ -64,6 +64,24 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
 int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
                              vg_stream_t stream);
 
+/* GEMM on host-resident (pinned) operands with copy/compute overlap; no reference
+ * counterpart (the reference engine uploads once and times device-resident launches,
+ * include/engine.cuh:28-32). A pipeline owns three streams (upload, compute, download)
+ * and per-row-block events. vg_host_pipeline_gemm_f16 uploads B and then A in `chunks`
+ * row blocks into the caller's device buffers dA (M×K), dB (N×K), dC (M×N), runs the
+ * B200 GEMM per row block as soon as it has landed, downloads each C row block as soon
+ * as it is done, and makes `done_stream` wait for the last download. Consecutive calls
+ * overlap (uploads of call i+1 with downloads of call i). Host buffers must be pinned and
+ * are accessed asynchronously: leave hA/hB unmodified and do not read hC until
+ * `done_stream` has passed the call (e.g. cudaStreamSynchronize). The calling thread's
+ * current device must be the pipeline's device. Returns 0 or a cudaError_t code. */
+typedef struct vg_host_pipeline *vg_host_pipeline_t;
+vg_host_pipeline_t vg_host_pipeline_create(int device);
+void vg_host_pipeline_destroy(vg_host_pipeline_t pipeline);
+int vg_host_pipeline_gemm_f16(vg_host_pipeline_t pipeline, const void *hA, const void *hB, void *hC,
+                              void *dA, void *dB, void *dC, int M, int N, int K, int chunks,
+                              vg_stream_t done_stream);
+
 /* Validation build: the same main loop as `version`, fp32 C (no fp16 rounding), so
  * accumulation error can be judged separately from output quantisation. No
  * counterpart in the reference (its only check is fp16-vs-cuBLAS,

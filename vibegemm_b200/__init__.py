@@ -41,6 +41,9 @@ _SIGS = {
     "vg_raster_tile": (None, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2),
     "vg_b200_plan": (ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.c_size_t] * 3 + [ctypes.c_int] * 2
                      + [ctypes.POINTER(ctypes.c_int)]),
+    "vg_host_pipeline_create": (ctypes.c_void_p, [ctypes.c_int]),
+    "vg_host_pipeline_destroy": (None, [ctypes.c_void_p]),
+    "vg_host_pipeline_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
     "vg_backend_count": (ctypes.c_int, []),
     "vg_backend_name": (ctypes.c_char_p, [ctypes.c_int]),
     "vg_backend_run": (ctypes.c_int, [ctypes.c_char_p] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3),
@@ -166,6 +169,57 @@ def cublas_gemm(A, B, out=None, stream=None):
 
 
 AUTO = -1  # per-shape version choice (the default entry point's policy)
+
+
+class HostPipeline:
+    """C = A @ B.T for pinned HOST tensors, overlapping uploads, GEMMs and downloads.
+
+    Owns the device buffers (grown on demand) and the C pipeline (three streams). Each
+    call enqueues the work and makes `stream` (default: current) wait for the result;
+    synchronise that stream before reading `out`.
+    """
+
+    def __init__(self, device: Optional[int] = None, chunks: int = 4):
+        import torch
+        self.device = torch.cuda.current_device() if device is None else device
+        self.chunks = chunks
+        self._h = lib().vg_host_pipeline_create(self.device)
+        if not self._h:
+            raise VibeGemmError("vg_host_pipeline_create", -1)
+        self._bufs = {}
+
+    def _buf(self, name, shape):
+        import torch
+        t = self._bufs.get(name)
+        if t is None or t.shape != shape:
+            t = torch.empty(shape, dtype=torch.float16, device=f"cuda:{self.device}")
+            self._bufs[name] = t
+        return t
+
+    def gemm(self, A, B, out, stream=None):
+        M, K = A.shape
+        N = B.shape[0]
+        if A.is_cuda or B.is_cuda or out.is_cuda:
+            raise ValueError("HostPipeline takes host tensors")
+        if not (A.is_pinned() and B.is_pinned() and out.is_pinned()):
+            raise ValueError("host tensors must be pinned (pin_memory=True)")
+        dA, dB, dC = self._buf("A", (M, K)), self._buf("B", (N, K)), self._buf("C", (M, N))
+        code = lib().vg_host_pipeline_gemm_f16(self._h, A.data_ptr(), B.data_ptr(), out.data_ptr(),
+                                               dA.data_ptr(), dB.data_ptr(), dC.data_ptr(),
+                                               M, N, K, self.chunks, _stream_handle(stream))
+        _check(code, "vg_host_pipeline_gemm_f16")
+        return out
+
+    def close(self):
+        if self._h:
+            lib().vg_host_pipeline_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def versions() -> list[str]:

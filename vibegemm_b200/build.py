@@ -26,7 +26,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libvibegemm_b200.so"
 BIN = PKG / "bin" / "VibeGEMM"
 
-LIB_SOURCES = ["gemm_b200.cu", "cublas_backends.cu", "gemm_b200_backends.cu", "engine_capi.cu"]
+LIB_SOURCES = ["gemm_b200.cu", "cublas_backends.cu", "gemm_b200_backends.cu", "engine_capi.cu",
+               "host_pipeline.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-DHAS_B200", "-Xcompiler", "-fPIC",
          "--expt-relaxed-constexpr", "-I" + str(INCLUDE), "-I" + str(CSRC)]

@@ -116,28 +116,41 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
 
 __device__ unsigned int vg_status_word;
 
+// Back-off between barrier probes of the epilogue warps, which wait a whole main loop
+// (tens of microseconds) for each accumulator; the producer and MMA warps, whose waits
+// gate the tensor pipe, probe without sleeping.
+#ifndef VG_EPI_BACKOFF_NS
+#define VG_EPI_BACKOFF_NS 0
+#endif
+
 __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                       unsigned long long timeout_ns, unsigned code) {
+                                       unsigned long long timeout_ns, unsigned code,
+                                       unsigned backoff_ns) {
     const uint64_t t0 = ptx::global_timer_ns();
-    while (true) {
+    for (uint32_t it = 1;; ++it) {
         // Suspend in hardware (up to ~0.1 ms per probe) rather than spin.
         if (ptx::mbar_try_wait_sleep(bar, parity, 100000u))
             return true;
-        if (*abort_flag)
-            return false;
-        if (ptx::global_timer_ns() - t0 > timeout_ns) {
-            *abort_flag = 1;
-            atomicCAS(&vg_status_word, 0u, code);
-            return false;
+        if (backoff_ns)
+            __nanosleep(backoff_ns);
+        if ((it & 7u) == 0) {
+            if (*abort_flag)
+                return false;
+            if (ptx::global_timer_ns() - t0 > timeout_ns) {
+                *abort_flag = 1;
+                atomicCAS(&vg_status_word, 0u, code);
+                return false;
+            }
         }
     }
 }
 
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                         unsigned long long timeout_ns, unsigned code) {
+                                         unsigned long long timeout_ns, unsigned code,
+                                         unsigned backoff_ns = 0) {
     if (ptx::mbar_try_wait(bar, parity))
         return true;
-    return wait_slow(bar, parity, abort_flag, timeout_ns, code);
+    return wait_slow(bar, parity, abort_flag, timeout_ns, code, backoff_ns);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(uint32_t lo_bits, uint32_t hi_bits) {
@@ -409,7 +422,8 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         for (int t = cluster_id; t < total_tiles; t += num_clusters) {
             int tm, tn;
             raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, tm, tn);
-            if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue))
+            if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
+                          VG_EPI_BACKOFF_NS))
                 break;
             ptx::tc_fence_after();
             const int row0 = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
