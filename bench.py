@@ -64,7 +64,9 @@ def parse_args():
     ap.add_argument("--version", type=int, default=None, help="kernel version (default: the per-shape choice of vg_b200_gemm_f16)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of C (N>1)")
+    ap.add_argument("--allgather", choices=["none", "nccl", "fused"], default="none",
+                    help="N>1: also time the all-gather of C, as a separate NCCL all-gather after "
+                         "the GEMM (nccl) or fused into the GEMM kernel's epilogue over NVLink (fused)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm8192")
     return ap.parse_args()
 
@@ -335,13 +337,38 @@ def run_b200(args) -> None:
                    "GEMM per block, C -> pinned host; steps overlap uploads and downloads"}
 
     allgather = None
-    if args.allgather and world > 1:
+    if args.allgather == "nccl" and world > 1:
         def gather_step():
             sh.gather(C)
         ms_ag = max_over_ranks(timed(gather_step, min(args.steps, 20), 3))
-        allgather = {"ms_per_step": ms_ag, "bytes_gathered": M * N_DIM * 2,
+        allgather = {"mode": "nccl", "ms_per_step": ms_ag, "bytes_gathered": M * N_DIM * 2,
                      "gemm_plus_allgather_value": flop_step / ((ms + ms_ag) * 1e-3) / 1e12,
                      "note": "NCCL all_gather_into_tensor of the row-major C shards, timed after the GEMM"}
+    elif args.allgather == "fused" and world > 1:
+        from vibegemm_b200.mgpu import FusedAllGatherGemm
+        fused = FusedAllGatherGemm(M, N_DIM, K_DIM, rank, world)
+
+        def fused_step():
+            fused.run(A, B, stream=stream)
+
+        ms_fused = max_over_ranks(timed(fused_step, args.steps, 3))
+        fused.barrier()
+        # Check: the rows gathered from the next rank equal that rank's GEMM, recomputed here
+        # from the same seeded generator.
+        peer = (rank + 1) % world
+        p0, prow = sh.__class__(M, N_DIM, K_DIM, peer, world).local
+        gen.manual_seed(42 + peer)
+        A_peer = torch.empty((prow, K_DIM), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=gen)
+        want = vg.gemm(A_peer, B)
+        torch.cuda.synchronize()
+        ok_rows = bool(torch.equal(fused.C[p0:p0 + prow], want))
+        ok_all = max_over_ranks(0.0 if ok_rows else 1.0) == 0.0
+        allgather = {"mode": "fused", "ms_per_step": ms_fused, "bytes_gathered": M * N_DIM * 2,
+                     "gemm_plus_allgather_value": flop_step / (ms_fused * 1e-3) / 1e12,
+                     "gathered_rows_exact": ok_all,
+                     "note": "one kernel per rank: the epilogue stores each C tile into every "
+                             "rank's full C over NVLink (symmetric memory peer pointers)"}
+        del fused
 
     pk = peaks()
     per_gpu_launch_tflops = 2.0 * rows * N_DIM * K_DIM / (ms_local * 1e-3) / 1e12

@@ -126,6 +126,20 @@ int vg_b200_set_wait_timeout_ns(unsigned long long ns); /* 0 restores the defaul
  * `timeout_ns`; returns 1 if the wait correctly gave up and recorded its status. */
 int vg_b200_selftest_wait_timeout(unsigned long long timeout_ns);
 
+/* Row-sharded GEMM fused with the all-gather of C (no reference counterpart; the
+ * reference is single-GPU). Rank `rank` of `world` (<= 8 GPUs of one NVLink domain)
+ * computes rows [row0, row0 + M_local) of C = A · B^T from its A rows (A_local, M_local×K)
+ * and the replicated B, and its epilogue writes every finished C tile both into its own
+ * full-size C (C_ranks[rank]) and, over NVLink, into every other rank's full-size C:
+ * C_ranks[r] must be rank r's M×N C buffer mapped into this process (peer pointers, e.g.
+ * from symmetric memory), N % 8 == 0 and 16-B aligned rows. The all-gather's traffic
+ * overlaps the math tile by tile. No kernel waits on another GPU: after the call, the
+ * ranks must synchronise (e.g. a barrier) before reading rows written by peers.
+ * Returns 0 or a cudaError_t code. */
+int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks, int world,
+                               int rank, long long row0, int M_local, int N, int K,
+                               vg_stream_t stream);
+
 /* Contiguous row-block sharding used by the multi-GPU driver (A and C split by rows,
  * B replicated): rank r of `world` owns rows [row0, row0 + rows). No reference
  * counterpart (the reference is single-device, main.cu:70). */

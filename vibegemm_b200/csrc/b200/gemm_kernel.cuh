@@ -47,7 +47,10 @@ enum EpiKind : int {
     kEpiTmaF16 = 0,    // smem staging + TMA store (C 16-B aligned, ldc % 8 == 0)
     kEpiDirectF16 = 1, // predicated global stores (any C alignment / ldc)
     kEpiDirectF32 = 2, // fp32 output, validation build of the same main loop
+    kEpiTmaF16Peers = 3, // TMA store to local C + the same rows into every peer GPU's C
 };
+
+constexpr int kMaxPeers = 7; // peers of one node (8 GPUs per NVSwitch domain)
 
 // Status codes written to vg_status_word (first writer wins).
 enum StatusCode : unsigned {
@@ -69,6 +72,9 @@ struct GemmArgs {
     void *C;         // direct epilogues only
     long long ldc;   // elements
     unsigned long long timeout_ns;
+    // kEpiTmaF16Peers: peer GPUs' copies of this shard's rows (row 0 of the shard, ld = ldc).
+    void *peers[kMaxPeers];
+    int num_peers;
 };
 
 template <int CG, int BN_> struct TileCfg {
@@ -105,7 +111,8 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
     static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
-    static constexpr int EPI_BYTES = (EPI == kEpiTmaF16) ? T::EPI_WARPS * 2 * T::STG_BYTES : 0;
+    static constexpr int EPI_BYTES =
+        (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) ? T::EPI_WARPS * 2 * T::STG_BYTES : 0;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
     static constexpr int SLOT_OFF = BAR_OFF + 8 * NUM_BARS;
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     if (warp == 0 && lane == 0) {
         ptx::prefetch_tmap(&mapA);
         ptx::prefetch_tmap(&mapB);
-        if (EPI == kEpiTmaF16)
+        if (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers)
             ptx::prefetch_tmap(&mapC);
     }
     if (warp == 1) {
@@ -450,7 +457,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                     }
                 }
                 const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
-                if constexpr (EPI == kEpiTmaF16) {
+                if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
                     uint32_t p[32];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
@@ -476,6 +483,29 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         if (row0 < args.M && ccol < args.N)
                             ptx::tma_store_2d(&mapC, stg, ccol, row0);
                         ptx::bulk_commit_group();
+                    }
+                    if constexpr (EPI == kEpiTmaF16Peers) {
+                        // Fused all-gather: the staged 32 × 64 box goes to every peer's C
+                        // over NVLink, eight lanes per row so that each row leaves as one
+                        // contiguous 128-B write (reads undo the 128-B swizzle).
+                        const int sub_row = lane >> 3, j = lane & 7;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = i * 4 + sub_row;
+                            const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
+                                               (static_cast<uint32_t>(j ^ (r & 7)) << 4);
+                            uint4 q;
+                            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                         : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                                         : "r"(a));
+                            const int grow = row0 + r;
+                            const int gcol = ccol + 8 * j;
+                            if (grow < args.M && gcol < args.N) {
+                                const long long off = static_cast<long long>(grow) * args.ldc + gcol;
+                                for (int pr = 0; pr < args.num_peers; ++pr)
+                                    *reinterpret_cast<uint4 *>(static_cast<__half *>(args.peers[pr]) + off) = q;
+                            }
+                        }
                     }
                     buf ^= 1;
                 } else if constexpr (EPI == kEpiDirectF16) {
@@ -534,10 +564,12 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 acc_phase ^= 1u;
             }
         }
-        if constexpr (EPI == kEpiTmaF16) {
+        if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
             if (lane == 0)
                 ptx::bulk_wait_group<0>();
         }
+        if constexpr (EPI == kEpiTmaF16Peers)
+            __threadfence_system(); // peer stores visible before the kernel's completion
         ptx::tc_fence_before();
     }
 

@@ -108,7 +108,7 @@ inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
 
 // Pure host planning (no CUDA calls): what the launcher will do for this problem.
 int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C, bool f32_out,
-              int num_sms, int max_clusters, Plan &p) {
+              int num_sms, int max_clusters, Plan &p, bool peers = false) {
     if (M < 0 || N < 0 || K < 0 || num_sms <= 0)
         return cudaErrorInvalidValue;
     if (version == kAutoVersion)
@@ -126,7 +126,12 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.pad_a = (K % 8 != 0) || !aligned16(A);
     p.pad_b = (K % 8 != 0) || !aligned16(B);
     p.Kp = (K % 8 == 0) ? K : (K + 7) / 8 * 8;
-    if (f32_out)
+    if (peers) {
+        // Fused all-gather: TMA-store epilogue plus 16-B peer stores (C rows 16-B aligned).
+        if (f32_out || !v.tma_store || N % 8 != 0 || !aligned16(C))
+            return cudaErrorInvalidValue;
+        p.epi = kEpiTmaF16Peers;
+    } else if (f32_out)
         p.epi = kEpiDirectF32;
     else if (v.tma_store && N % 8 == 0 && aligned16(C))
         p.epi = kEpiTmaF16;
@@ -380,6 +385,7 @@ cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
         VG_EPI_CASE(kEpiTmaF16)
         VG_EPI_CASE(kEpiDirectF16)
         VG_EPI_CASE(kEpiDirectF32)
+        VG_EPI_CASE(kEpiTmaF16Peers)
     default:
         return cudaErrorInvalidValue;
     }
@@ -399,7 +405,7 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
 }
 
 cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
-                     bool f32_out, cudaStream_t s) {
+                     bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0) {
     if ((version != kAutoVersion && (version < 0 || version >= kNumVersions)) || M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
@@ -422,9 +428,14 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     if (di->major != 10 || di->minor != 0)
         return cudaErrorNoKernelImageForDevice;
 
+    if (num_peers < 0 || num_peers > kMaxPeers)
+        return cudaErrorInvalidValue;
+    for (int i = 0; i < num_peers; ++i)
+        if (!peers || !peers[i] || !aligned16((uintptr_t)peers[i]))
+            return cudaErrorInvalidValue;
     Plan p;
     e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, f32_out,
-                               di->num_sms, di->num_sms / 2, p);
+                               di->num_sms, di->num_sms / 2, p, num_peers > 0);
     if (e != cudaSuccess)
         return e;
 
@@ -468,7 +479,7 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     const uint32_t b_box_rows = (uint32_t)(p.bn / p.cta_group);
     bool ok = get_map(ma, A_use, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp, 64u, 128u, dev) &&
               get_map(mb, B_use, (uint64_t)Kp, (uint64_t)N, (uint64_t)Kp, 64u, b_box_rows, dev);
-    if (ok && p.epi == kEpiTmaF16)
+    if (ok && (p.epi == kEpiTmaF16 || p.epi == kEpiTmaF16Peers))
         ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
     if (!ok) {
         if (ws)
@@ -488,6 +499,9 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     args.C = C;
     args.ldc = N;
     args.timeout_ns = wait_timeout_ns();
+    args.num_peers = num_peers;
+    for (int i = 0; i < num_peers; ++i)
+        args.peers[i] = peers[i];
 
     e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
     if (ws) {
@@ -641,6 +655,26 @@ int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C,
 int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
                              vg_stream_t stream) {
     return vg::run_gemm_noalloc(A, B, C, M, N, K, (cudaStream_t)stream);
+}
+
+int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks, int world,
+                               int rank, long long row0, int M_local, int N, int K,
+                               vg_stream_t stream) {
+    if (!C_ranks || world < 1 || world > vg::kMaxPeers + 1 || rank < 0 || rank >= world || row0 < 0 ||
+        M_local < 0 || N < 0)
+        return (int)cudaErrorInvalidValue;
+    const size_t off = (size_t)row0 * (size_t)N * sizeof(__half);
+    void *peers[vg::kMaxPeers];
+    int np = 0;
+    for (int r = 0; r < world; ++r) {
+        if (!C_ranks[r])
+            return (int)cudaErrorInvalidValue;
+        if (r != rank)
+            peers[np++] = static_cast<char *>(C_ranks[r]) + off;
+    }
+    void *C_local = static_cast<char *>(C_ranks[rank]) + off;
+    return (int)vg::run_gemm(vg::kAutoVersion, A_local, B, C_local, M_local, N, K, false,
+                             (cudaStream_t)stream, peers, np);
 }
 
 int vg_b200_num_versions(void) { return vg::kNumVersions; }

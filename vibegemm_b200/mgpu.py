@@ -9,6 +9,12 @@ copy-free because the row-major C shards are contiguous slices of the full C
 
 The compute step is a parameter (``gemm_fn``): the B200 kernel on GPUs, the CPU oracle in
 the world-size-2 gloo tests of this host logic.
+
+``FusedAllGatherGemm`` replaces GEMM-then-all-gather by one kernel per rank
+(``vg_b200_gemm_f16_allgather``): its epilogue writes every finished C tile into the full C
+of every rank over NVLink while the tensor cores work on the next tile. The full-size C
+buffers live in symmetric memory (torch's allocator maps each rank's buffer into every
+peer's address space); torch is only the allocator and the barrier here.
 """
 from __future__ import annotations
 
@@ -62,3 +68,43 @@ class RowShardedGemm:
         full = torch.empty((blk * self.world, self.N), dtype=C_local.dtype, device=C_local.device)
         dist.all_gather_into_tensor(full, send.contiguous(), group=group)
         return full[: self.M]
+
+
+class FusedAllGatherGemm:
+    """Row-sharded GEMM with the all-gather of C fused into the kernel's epilogue.
+
+    Every rank holds the full C (``self.C[:M]``, padded to world × block rows so all ranks
+    allocate the same size) in symmetric memory. ``run`` launches the fused kernel on the
+    current stream; call ``barrier`` before reading rows written by other ranks.
+    """
+
+    def __init__(self, M: int, N: int, K: int, rank: int, world: int, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        self.sh = RowShardedGemm(M, N, K, rank, world)
+        self.rank, self.world = rank, world
+        self.group = group if group is not None else dist.group.WORLD
+        blk = self.sh.block_rows
+        self.C_full = symm.empty((blk * world, N), dtype=torch.float16, device=torch.cuda.current_device())
+        self.handle = symm.rendezvous(self.C_full, self.group)
+        base = self.handle.buffer_ptrs[rank]
+        offset = self.C_full.data_ptr() - base
+        self.c_rank_ptrs = [int(p) + offset for p in self.handle.buffer_ptrs]
+
+    @property
+    def C(self):
+        return self.C_full[: self.sh.M]
+
+    def run(self, A_local, B, stream=None) -> None:
+        import vibegemm_b200 as vg
+        r0, rows = self.sh.local
+        if rows > 0:
+            vg.gemm_allgather(A_local, B, self.c_rank_ptrs, self.rank, r0, stream)
+
+    def barrier(self) -> None:
+        import torch
+        import torch.distributed as dist
+        dist.barrier(group=self.group)
+        torch.cuda.synchronize()
