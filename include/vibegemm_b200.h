@@ -50,15 +50,18 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
  * (needed when K % 8 != 0 or A/B is not 16-byte aligned) from the CUDA stream-ordered
  * pool; this entry point uses a fixed 32 MiB array in the library's device memory
  * instead and never calls cudaMalloc, cudaMallocAsync, cudaFree or an allocating library.
- *   - Limit: the padded copies (M + N) * roundup(K, 8) * 2 bytes must fit in 32 MiB;
- *     larger padded problems return VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing.
- *     Problems that need no padding have no size limit.
+ *   - Limit: the call's workspace must fit in 32 MiB: the padded copies
+ *     (M + N) * roundup(K, 8) * 2 bytes, plus for small grids that use stream-K scheduling
+ *     the fp32 partial tiles (at most 148 * 128 KB = 18.5 MiB). Larger workspaces return
+ *     VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing. Problems that need neither have
+ *     no size limit.
  *   - The 32 MiB are held on every GPU that loads the library until the process exits.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - All calls share the array: calls that overlap on the GPU (different streams, or
  *     different host threads on one device) race on it; serialise them. Each call
- *     rewrites every scratch byte it reads, so no clearing is needed between calls.
+ *     rewrites every scratch byte it reads and zeroes its stream-K flags itself
+ *     (cudaMemsetAsync), so nothing needs clearing between calls.
  * Same semantics, arguments and return codes as vg_b200_gemm_f16 otherwise. */
 #define VG_ERROR_NOALLOC_SCRATCH_LIMIT 2001
 int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
@@ -149,12 +152,22 @@ void vg_shard_rows(long long M, int world, int rank, long long *row0, long long 
  * (tile_m, tile_n). Replaces Schedule::next (csrc/h100/gemm_8192x8192_v18.cuh:207-260). */
 void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *tile_n);
 
+/* Work units persistent worker `worker` of `workers` processes (host copy of the device
+ * schedule, for tests): data-parallel (stream_k = 0: whole tiles in grouped-raster order)
+ * or stream-K (stream_k = 1: an equal share of the (tile, k-block) iterations). Writes up
+ * to max_units records of 7 ints {tile_m, tile_n, kb0, kb1, kind (0 whole tile, 1 partial
+ * written to the workspace, 2 owner that adds the partials of workers first..last),
+ * first_contrib, last_contrib} and returns the number of units (-1 on bad input).
+ * Replaces the tile walk of Schedule::next (csrc/h100/gemm_8192x8192_v18.cuh:207-260). */
+int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, int group_m,
+                  int num_kb, int *out, int max_units);
+
 /* Host-side launch plan for a problem, as the launcher would build it for a device
  * with `num_sms` SMs (exposed so the planner can be tested without a GPU).
- * `version` may be -1 (per-shape choice). Fields of `out` (int[14]): cta_group, stages,
- * epilogue kind (0 TMA fp16, 1 direct fp16, 2 direct fp32), pad_a, pad_b, padded K,
- * num_m_tiles, num_n_tiles, num_kb, group_m, grid (CTAs), persistent, tile columns,
- * resolved version. Returns 0 or a cudaError_t code. */
+ * `version` may be -1 (per-shape choice). Fields of `out` (int[15]): cta_group, stages,
+ * epilogue kind (0 TMA fp16, 1 direct fp16, 2 direct fp32, 3 TMA fp16 + peer stores),
+ * pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb, group_m, grid (CTAs),
+ * persistent, tile columns, resolved version, stream-K. Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int f32_out, int num_sms, int *out);
 

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol(vg):
 
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
-                             "VibeGEMM B200 v3"]
+                             "VibeGEMM B200 v3", "VibeGEMM B200 v4"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -82,7 +82,7 @@ def test_plan_aligned_square(vg):
     ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 3), ((4096, 14336, 4096), 3),
     ((4096, 4096, 14336), 3), ((8191, 8193, 4099), 3),
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
-    ((1000, 3000, 2048), 1),     # fewer pair tiles than pair slots: single-CTA tiles
+    ((1000, 3000, 2048), 4),     # fewer pair tiles than pair slots: stream-K
     ((512, 512, 512), 1),
 ])
 def test_auto_version_choice(vg, shape, want):

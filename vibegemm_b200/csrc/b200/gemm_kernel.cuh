@@ -59,6 +59,7 @@ enum StatusCode : unsigned {
     kStatusTimeoutMma = 0x102,
     kStatusTimeoutEpilogue = 0x103,
     kStatusTimeoutDrain = 0x104,
+    kStatusTimeoutPartial = 0x105,
     kStatusTimeoutSelftest = 0x1FF,
 };
 
@@ -75,6 +76,10 @@ struct GemmArgs {
     // kEpiTmaF16Peers: peer GPUs' copies of this shard's rows (row 0 of the shard, ld = ldc).
     void *peers[kMaxPeers];
     int num_peers;
+    // Stream-K: per-(worker, CTA rank) fp32 partial slots (128 × BN floats each, in TMEM
+    // lane order) and ready flags (zeroed before the launch).
+    float *sk_partials;
+    unsigned *sk_flags;
 };
 
 template <int CG, int BN_> struct TileCfg {
@@ -165,7 +170,32 @@ __device__ __forceinline__ uint32_t pack_half2(uint32_t lo_bits, uint32_t hi_bit
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-template <int CG, int BN, int STAGES, int EPI>
+// Waits (bounded) until flag `f` reads nonzero, with GPU-scope acquire.
+__device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort_flag,
+                                          unsigned long long timeout_ns) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v)
+        return true;
+    const uint64_t t0 = ptx::global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v)
+            return true;
+        if ((it & 15u) == 0) {
+            if (*abort_flag)
+                return false;
+            if (ptx::global_timer_ns() - t0 > timeout_ns) {
+                *abort_flag = 1;
+                atomicCAS(&vg_status_word, 0u, (unsigned)kStatusTimeoutPartial);
+                return false;
+            }
+        }
+    }
+}
+
+template <int CG, int BN, int STAGES, int EPI, bool SK = false>
 __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
@@ -230,7 +260,6 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
 
     const int cluster_id = static_cast<int>(blockIdx.x) / CG;
     const int num_clusters = static_cast<int>(gridDim.x) / CG;
-    const int total_tiles = args.num_m_tiles * args.num_n_tiles;
     const unsigned long long tmo = args.timeout_ns;
 
     if (warp == 0) {
@@ -240,12 +269,14 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-                int tm, tn;
-                raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, tm, tn);
-                const int a_row = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM;
-                const int b_row = tn * T::BN + static_cast<int>(rank) * T::B_ROWS;
-                for (int kb = 0; kb < args.num_kb; ++kb) {
+            UnitIter it;
+            it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                    args.num_kb);
+            WorkUnit u;
+            while (ok && it.next(u)) {
+                const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
+                const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
+                for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
                                   kStatusTimeoutProducer)) {
                         ok = false;
@@ -324,7 +355,12 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 else
                     ptx::mma_commit_pair(bar, 0x3);
             };
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+            UnitIter it;
+            it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                    args.num_kb);
+            WorkUnit u;
+            while (ok && it.next(u)) {
+                const int nkb = u.kb1 - u.kb0; // k-blocks of this unit; MMAs index them from 0
                 if constexpr (T::ACC_BUFS == 2) {
                     if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
                                   kStatusTimeoutMma)) {
@@ -333,7 +369,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                     }
                     ptx::tc_fence_after();
                     const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::BN);
-                    for (int kb = 0; kb < args.num_kb; ++kb) {
+                    for (int kb = 0; kb < nkb; ++kb) {
                         if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                             ok = false;
                             break;
@@ -358,7 +394,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         break;
                     }
                     ptx::tc_fence_after();
-                    const int run = args.num_kb < STAGES ? args.num_kb : STAGES;
+                    const int run = nkb < STAGES ? nkb : STAGES;
                     const int s0 = stage;
                     const uint32_t p0 = phase;
                     for (int kb = 0; kb < run; ++kb) {
@@ -385,7 +421,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         commit_to(empty_bar(stage));
                         advance();
                     }
-                    for (int kb = run; kb < args.num_kb; ++kb) {
+                    for (int kb = run; kb < nkb; ++kb) {
                         if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                             ok = false;
                             break;
@@ -426,15 +462,29 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int buf = 0;
-        for (int t = cluster_id; t < total_tiles; t += num_clusters) {
-            int tm, tn;
-            raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, tm, tn);
+        UnitIter it;
+        it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                args.num_kb);
+        WorkUnit u;
+        // Stream-K partial slot of (worker, CTA rank), TMEM lane order: [BN/32][128][32] floats.
+        auto slot_of = [&](int worker) {
+            return args.sk_partials + static_cast<long long>(worker * CG + static_cast<int>(rank)) *
+                                          (T::BM * T::BN);
+        };
+        bool epi_ok = true;
+        while (epi_ok && it.next(u)) {
             if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
                           VG_EPI_BACKOFF_NS))
                 break;
             ptx::tc_fence_after();
-            const int row0 = tm * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
-            const int col0 = tn * T::BN;
+            const int row0 = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
+            const int col0 = u.tile_n * T::BN;
+            // Owner of a split tile: the contributors' partials must have landed.
+            if (SK && u.kind == kUnitOwner) {
+                for (int c = u.first_contrib; c <= u.last_contrib && epi_ok; ++c)
+                    epi_ok = wait_flag(args.sk_flags + c * CG + rank, abort_flag, tmo);
+                __syncwarp();
+            }
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * 256);
 #pragma unroll 1
@@ -457,6 +507,39 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                     }
                 }
                 const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
+                if constexpr (SK) {
+                    const long long lane_off = (static_cast<long long>(sub) * 32 + lane) * 32;
+                    if (u.kind == kUnitPartial) {
+                        // Park the fp32 accumulator: each lane writes its row's 2 × 32 floats,
+                        // a warp 2 × 4 KB contiguous.
+                        float *dst = slot_of(it.w) + static_cast<long long>(2 * c) * (T::BM * 32) + lane_off;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            reinterpret_cast<uint4 *>(dst)[q] = make_uint4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
+                            reinterpret_cast<uint4 *>(dst + T::BM * 32)[q] =
+                                make_uint4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]);
+                        }
+                        continue;
+                    }
+                    if (u.kind == kUnitOwner && epi_ok) {
+                        for (int w2 = u.first_contrib; w2 <= u.last_contrib; ++w2) {
+                            const float *src = slot_of(w2) + static_cast<long long>(2 * c) * (T::BM * 32) + lane_off;
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const float4 a = reinterpret_cast<const float4 *>(src)[q];
+                                const float4 b = reinterpret_cast<const float4 *>(src + T::BM * 32)[q];
+                                v0[4 * q] = __float_as_uint(__uint_as_float(v0[4 * q]) + a.x);
+                                v0[4 * q + 1] = __float_as_uint(__uint_as_float(v0[4 * q + 1]) + a.y);
+                                v0[4 * q + 2] = __float_as_uint(__uint_as_float(v0[4 * q + 2]) + a.z);
+                                v0[4 * q + 3] = __float_as_uint(__uint_as_float(v0[4 * q + 3]) + a.w);
+                                v1[4 * q] = __float_as_uint(__uint_as_float(v1[4 * q]) + b.x);
+                                v1[4 * q + 1] = __float_as_uint(__uint_as_float(v1[4 * q + 1]) + b.y);
+                                v1[4 * q + 2] = __float_as_uint(__uint_as_float(v1[4 * q + 2]) + b.z);
+                                v1[4 * q + 3] = __float_as_uint(__uint_as_float(v1[4 * q + 3]) + b.w);
+                            }
+                        }
+                    }
+                }
                 if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
                     uint32_t p[32];
 #pragma unroll
@@ -554,6 +637,16 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             }
                         }
                     }
+                }
+            }
+            if (SK && u.kind == kUnitPartial) {
+                // All epilogue warps' partial stores, then one release of the ready flag.
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * T::EPI_WARPS) : "memory");
+                if (warp == 2 && lane == 0) {
+                    __threadfence();
+                    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(args.sk_flags + it.w * CG + rank),
+                                 "r"(1u)
+                                 : "memory");
                 }
             }
             if constexpr (T::ACC_BUFS == 2) {

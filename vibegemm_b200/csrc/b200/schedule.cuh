@@ -34,6 +34,83 @@ VG_HD void raster_tile(int t, int num_m, int num_n, int group_m, int &tile_m, in
     tile_n = r / gsize;
 }
 
+// ── work units of the persistent workers ──────────────────────────────────────
+// A unit is tile (tile_m, tile_n) restricted to k-blocks [kb0, kb1).
+//   data-parallel: worker w takes whole tiles w, w+P, w+2P, ... (grouped raster).
+//   stream-K:      the T·KB (tile, k-block) iterations are cut into P equal contiguous
+//                  ranges, [w·W/P, (w+1)·W/P) with W = T·KB, walked in order. A unit that
+//                  starts inside a tile (kb0 > 0) is PARTIAL: its fp32 accumulator goes to
+//                  workspace slot w. A unit that holds a split tile's k-block 0 is the
+//                  OWNER: it adds the partials of workers first_contrib..last_contrib and
+//                  stores C. A worker's partial unit can only be its first unit and its
+//                  owner unit only its last, so an owner waits only on later workers'
+//                  first units: no cycle.
+enum UnitKind : int { kUnitFull = 0, kUnitPartial = 1, kUnitOwner = 2 };
+
+struct WorkUnit {
+    int tile_m, tile_n, kb0, kb1, kind;
+    int first_contrib, last_contrib; // owner units: workers holding the other k-blocks
+};
+
+struct UnitIter {
+    bool sk;
+    int w, P, num_m, num_n, group_m, KB;
+    long long i, end, W; // stream-K position
+    int t;               // data-parallel position
+
+    VG_HD void init(bool stream_k, int worker, int workers, int nm, int nn, int gm, int kb) {
+        sk = stream_k;
+        w = worker;
+        P = workers;
+        num_m = nm;
+        num_n = nn;
+        group_m = gm;
+        KB = kb;
+        W = (long long)nm * nn * kb;
+        i = begin_of(w);
+        end = begin_of(w + 1);
+        t = w;
+    }
+    VG_HD long long begin_of(int worker) const { return (long long)worker * W / P; }
+    // Worker whose range contains iteration index `idx`.
+    VG_HD int worker_of(long long idx) const { return (int)(((idx + 1) * P + W - 1) / W) - 1; }
+
+    VG_HD bool next(WorkUnit &u) {
+        if (!sk) {
+            if (t >= num_m * num_n)
+                return false;
+            raster_tile(t, num_m, num_n, group_m, u.tile_m, u.tile_n);
+            u.kb0 = 0;
+            u.kb1 = KB;
+            u.kind = kUnitFull;
+            u.first_contrib = u.last_contrib = -1;
+            t += P;
+            return true;
+        }
+        if (i >= end)
+            return false;
+        const int tile = (int)(i / KB);
+        const int k0 = (int)(i % KB);
+        const long long left = end - i;
+        const int k1 = (k0 + left < KB) ? (int)(k0 + left) : KB;
+        raster_tile(tile, num_m, num_n, group_m, u.tile_m, u.tile_n);
+        u.kb0 = k0;
+        u.kb1 = k1;
+        u.first_contrib = u.last_contrib = -1;
+        if (k0 == 0 && k1 == KB) {
+            u.kind = kUnitFull;
+        } else if (k0 == 0) {
+            u.kind = kUnitOwner;
+            u.first_contrib = w + 1;
+            u.last_contrib = worker_of((long long)(tile + 1) * KB - 1);
+        } else {
+            u.kind = kUnitPartial;
+        }
+        i += k1 - k0;
+        return true;
+    }
+};
+
 // Contiguous row-block shard of M rows over `world` ranks: rank r owns rows
 // [r*ceil(M/world), min(M, (r+1)*ceil(M/world))). Ranks past the end own 0 rows.
 VG_HD void shard_rows(long long M, int world, int rank, long long &row0, long long &rows) {

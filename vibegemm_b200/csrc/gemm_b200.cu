@@ -13,6 +13,10 @@
 //       4-stage ring of 48 KB, per-half TMEM hand-back with half-0 run-ahead: 3/4 of
 //       v2's L2→SMEM bytes and half its TMA loads per FLOP. Under the 1 kW power cap
 //       the lower data movement keeps the SM clock ~15 % higher than v2's.
+//   v4  v2's CTA-pair kernel with stream-K scheduling: the (tile, k-block) iterations
+//       are split evenly over the co-resident pairs; split tiles are finished by the
+//       pair holding k-block 0 from fp32 partials in a workspace. For grids with fewer
+//       tiles than pair slots.
 //   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
@@ -46,6 +50,7 @@ struct VersionDesc {
     bool persistent;
     bool tma_store;
     int group_m;
+    bool stream_k = false;
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -53,6 +58,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v1", 1, 256, 4, true, true, 8},
     {"VibeGEMM B200 v2", 2, 256, 6, true, true, 8},
     {"VibeGEMM B200 v3", 2, 512, 4, true, true, 16},
+    {"VibeGEMM B200 v4", 2, 256, 6, true, true, 8, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -62,16 +68,23 @@ constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's 
 // full wave of pair tiles; short K (< 1024) favours the double-buffered 256×256 pair
 // (v2), whose epilogue fully overlaps the next tile; grids too small to fill the
 // pairs favour 128×256 single-CTA tiles (v1), which occupy twice as many SMs.
+// Grids with fewer 256×256 tiles than pair slots but enough k-blocks to give every pair
+// at least 4 go to stream-K (v4), which keeps all pairs busy.
 int select_version(int M, int N, int K, int num_sms) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
+    const long long kb = ceil_div_i(K, 64);
     if (K >= 1024 && t3 >= pairs)
         return 3;
     if (t2 >= pairs)
         return 2;
+    if (t2 * kb >= 4 * pairs)
+        return 4;
     return 1;
 }
+
+constexpr int kMinSkIters = 4; // k-blocks per stream-K worker at least
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
 
@@ -92,6 +105,7 @@ int raster_group_override() {
 
 struct Plan {
     int version = 0; // resolved version (never kAutoVersion)
+    int stream_k = 0;
     int cta_group = 1;
     int bn = 256;
     int stages = 4;
@@ -141,7 +155,15 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.num_n_tiles = ceil_div_i(N, v.bn);
     p.num_kb = ceil_div_i(p.Kp, 64);
     const long long tiles = (long long)p.num_m_tiles * p.num_n_tiles;
-    if (v.persistent) {
+    p.stream_k = v.stream_k ? 1 : 0;
+    if (v.stream_k) {
+        if (peers)
+            return cudaErrorInvalidValue;
+        const int slots = (v.cta_group == 2) ? std::max(1, max_clusters) : num_sms;
+        const long long iters = tiles * p.num_kb;
+        const long long workers = std::max(1LL, std::min<long long>(slots, iters / kMinSkIters));
+        p.grid = (int)workers * v.cta_group;
+    } else if (v.persistent) {
         const int slots = (v.cta_group == 2) ? std::max(1, max_clusters) : num_sms;
         p.grid = (int)std::min<long long>(tiles, slots) * v.cta_group;
     } else {
@@ -308,7 +330,7 @@ cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, i
 }
 
 // ── kernel launch ────────────────────────────────────────────────────────────
-template <int CG, int BN, int STAGES, int EPI> struct Inst {
+template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
     static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
     static std::atomic<unsigned long long> attr_ready; // bit per device
     static int max_clusters[kMaxDevices];
@@ -316,7 +338,7 @@ template <int CG, int BN, int STAGES, int EPI> struct Inst {
     static cudaError_t prepare(int dev) {
         if ((attr_ready.load(std::memory_order_acquire) >> dev) & 1ull)
             return cudaSuccess;
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
@@ -344,7 +366,7 @@ template <int CG, int BN, int STAGES, int EPI> struct Inst {
 
     static cudaError_t launch(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                               const GemmArgs &args, int grid, cudaStream_t s) {
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK>;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid, 1, 1);
         cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
@@ -362,32 +384,42 @@ template <int CG, int BN, int STAGES, int EPI> struct Inst {
         return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
     }
 };
-template <int CG, int BN, int STAGES, int EPI>
-std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI>::attr_ready{0};
-template <int CG, int BN, int STAGES, int EPI>
-int Inst<CG, BN, STAGES, EPI>::max_clusters[kMaxDevices] = {};
+template <int CG, int BN, int STAGES, int EPI, bool SK>
+std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK>::attr_ready{0};
+template <int CG, int BN, int STAGES, int EPI, bool SK>
+int Inst<CG, BN, STAGES, EPI, SK>::max_clusters[kMaxDevices] = {};
 
-template <int CG, int BN, int STAGES>
+template <int CG, int BN, int STAGES, bool SK = false>
 cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
                          const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                          const GemmArgs *args, int grid, cudaStream_t s) {
 #define VG_EPI_CASE(E)                                                                             \
     case E: {                                                                                      \
-        cudaError_t e = Inst<CG, BN, STAGES, E>::prepare(dev);                                     \
+        cudaError_t e = Inst<CG, BN, STAGES, E, SK>::prepare(dev);                                 \
         if (e != cudaSuccess)                                                                      \
             return e;                                                                              \
-        max_clusters = Inst<CG, BN, STAGES, E>::max_clusters[dev];                                 \
+        max_clusters = Inst<CG, BN, STAGES, E, SK>::max_clusters[dev];                             \
         if (query_only)                                                                            \
             return cudaSuccess;                                                                    \
-        return Inst<CG, BN, STAGES, E>::launch(*ma, *mb, *mc, *args, grid, s);                     \
+        return Inst<CG, BN, STAGES, E, SK>::launch(*ma, *mb, *mc, *args, grid, s);                 \
     }
-    switch (epi) {
-        VG_EPI_CASE(kEpiTmaF16)
-        VG_EPI_CASE(kEpiDirectF16)
-        VG_EPI_CASE(kEpiDirectF32)
-        VG_EPI_CASE(kEpiTmaF16Peers)
-    default:
-        return cudaErrorInvalidValue;
+    if constexpr (SK) {
+        switch (epi) {
+            VG_EPI_CASE(kEpiTmaF16)
+            VG_EPI_CASE(kEpiDirectF16)
+            VG_EPI_CASE(kEpiDirectF32)
+        default:
+            return cudaErrorInvalidValue;
+        }
+    } else {
+        switch (epi) {
+            VG_EPI_CASE(kEpiTmaF16)
+            VG_EPI_CASE(kEpiDirectF16)
+            VG_EPI_CASE(kEpiDirectF32)
+            VG_EPI_CASE(kEpiTmaF16Peers)
+        default:
+            return cudaErrorInvalidValue;
+        }
     }
 #undef VG_EPI_CASE
 }
@@ -397,11 +429,35 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
                      const GemmArgs *args, int grid, cudaStream_t s) {
     if (p.cta_group == 1 && p.bn == 256 && p.stages == 4)
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
-    if (p.cta_group == 2 && p.bn == 256 && p.stages == 6)
+    if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 2 && p.bn == 512 && p.stages == 4)
         return dispatch_epi<2, 512, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    if (p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
+        return dispatch_epi<2, 256, 6, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     return cudaErrorInvalidValue;
+}
+
+inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Byte layout of a call's workspace: padded A, padded B, stream-K partials, flags.
+struct WsLayout {
+    size_t a_off = 0, b_off = 0, part_off = 0, flag_off = 0, flag_bytes = 0, total = 0;
+};
+
+WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
+    WsLayout w;
+    const size_t a = p.pad_a ? round_up_256((size_t)M * p.Kp * sizeof(__half)) : 0;
+    const size_t b = p.pad_b ? round_up_256((size_t)N * p.Kp * sizeof(__half)) : 0;
+    const size_t slots = p.stream_k ? (size_t)grid : 0; // one per (worker, CTA rank)
+    const size_t part = slots * 128 * (size_t)p.bn * sizeof(float);
+    w.a_off = 0;
+    w.b_off = a;
+    w.part_off = a + b;
+    w.flag_off = a + b + part;
+    w.flag_bytes = round_up_256(slots * sizeof(unsigned));
+    w.total = (a + b + part + (slots ? w.flag_bytes : 0));
+    return w;
 }
 
 cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
@@ -448,18 +504,21 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     if (p.cta_group == 2 && p.persistent && max_clusters > 0)
         grid = std::min(grid, 2 * max_clusters);
 
-    // Operands TMA cannot describe go through a K-padded copy.
+    // One stream-ordered workspace: K-padded copies of operands TMA cannot describe, and
+    // the stream-K partial slots + ready flags (zeroed here, every launch).
     const void *A_use = A, *B_use = B;
     void *ws = nullptr;
     const int Kp = p.Kp;
-    if (p.pad_a || p.pad_b) {
-        const size_t a_bytes = p.pad_a ? (size_t)M * Kp * sizeof(__half) : 0;
-        const size_t b_bytes = p.pad_b ? (size_t)N * Kp * sizeof(__half) : 0;
-        e = cudaMallocAsync(&ws, a_bytes + b_bytes, s);
+    const WsLayout wl = workspace_layout(p, M, N, grid);
+    float *sk_partials = nullptr;
+    unsigned *sk_flags = nullptr;
+    if (wl.total) {
+        e = cudaMallocAsync(&ws, wl.total, s);
         if (e != cudaSuccess)
             return e;
-        __half *wa = static_cast<__half *>(ws);
-        __half *wb = reinterpret_cast<__half *>(static_cast<char *>(ws) + a_bytes);
+        char *base = static_cast<char *>(ws);
+        __half *wa = reinterpret_cast<__half *>(base + wl.a_off);
+        __half *wb = reinterpret_cast<__half *>(base + wl.b_off);
         if (p.pad_a) {
             e = launch_pad(A, M, K, wa, Kp, di->num_sms, s);
             A_use = wa;
@@ -467,6 +526,12 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
         if (e == cudaSuccess && p.pad_b) {
             e = launch_pad(B, N, K, wb, Kp, di->num_sms, s);
             B_use = wb;
+        }
+        if (p.stream_k) {
+            sk_partials = reinterpret_cast<float *>(base + wl.part_off);
+            sk_flags = reinterpret_cast<unsigned *>(base + wl.flag_off);
+            if (e == cudaSuccess)
+                e = cudaMemsetAsync(sk_flags, 0, wl.flag_bytes, s);
         }
         if (e != cudaSuccess) {
             (void)cudaFreeAsync(ws, s);
@@ -499,6 +564,8 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     args.C = C;
     args.ldc = N;
     args.timeout_ns = wait_timeout_ns();
+    args.sk_partials = sk_partials;
+    args.sk_flags = sk_flags;
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
@@ -540,8 +607,6 @@ const ScratchAddr &noalloc_scratch_addr(int dev) {
     return g_scratch[dev];
 }
 
-inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
-
 // Same plan, descriptors and launches as run_gemm for the default version, with the
 // K-padding workspace taken from noalloc_scratch; nothing is allocated or freed.
 // Returns a cudaError_t value or VG_ERROR_NOALLOC_SCRATCH_LIMIT.
@@ -574,11 +639,6 @@ int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
     if (e != cudaSuccess)
         return e;
     const int Kp = p.Kp;
-    const size_t a_bytes = p.pad_a ? round_up_256((size_t)M * Kp * sizeof(__half)) : 0;
-    const size_t b_bytes = p.pad_b ? (size_t)N * Kp * sizeof(__half) : 0;
-    if (a_bytes + b_bytes > kNoAllocScratchBytes)
-        return VG_ERROR_NOALLOC_SCRATCH_LIMIT;
-
     int max_clusters = 0;
     e = dispatch(p, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
     if (e != cudaSuccess)
@@ -586,14 +646,22 @@ int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
     int grid = p.grid;
     if (p.cta_group == 2 && p.persistent && max_clusters > 0)
         grid = std::min(grid, 2 * max_clusters);
+    // Same workspace as run_gemm (padded operands, stream-K partials and flags), placed in
+    // the fixed array; it must fit.
+    const WsLayout wl = workspace_layout(p, M, N, grid);
+    if (wl.total > kNoAllocScratchBytes)
+        return VG_ERROR_NOALLOC_SCRATCH_LIMIT;
 
     const void *A_use = A, *B_use = B;
-    if (p.pad_a || p.pad_b) {
+    float *sk_partials = nullptr;
+    unsigned *sk_flags = nullptr;
+    if (wl.total) {
         const ScratchAddr &sc = noalloc_scratch_addr(dev);
         if (sc.err != cudaSuccess)
             return sc.err;
-        __half *wa = static_cast<__half *>(sc.ptr);
-        __half *wb = reinterpret_cast<__half *>(static_cast<char *>(sc.ptr) + a_bytes);
+        char *base = static_cast<char *>(sc.ptr);
+        __half *wa = reinterpret_cast<__half *>(base + wl.a_off);
+        __half *wb = reinterpret_cast<__half *>(base + wl.b_off);
         if (p.pad_a) {
             e = launch_pad(A, M, K, wa, Kp, di->num_sms, s);
             A_use = wa;
@@ -601,6 +669,12 @@ int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
         if (e == cudaSuccess && p.pad_b) {
             e = launch_pad(B, N, K, wb, Kp, di->num_sms, s);
             B_use = wb;
+        }
+        if (p.stream_k) {
+            sk_partials = reinterpret_cast<float *>(base + wl.part_off);
+            sk_flags = reinterpret_cast<unsigned *>(base + wl.flag_off);
+            if (e == cudaSuccess) // flags start at zero every call (not an allocation)
+                e = cudaMemsetAsync(sk_flags, 0, wl.flag_bytes, s);
         }
         if (e != cudaSuccess)
             return e;
@@ -628,6 +702,8 @@ int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K,
     args.C = C;
     args.ldc = N;
     args.timeout_ns = wait_timeout_ns();
+    args.sk_partials = sk_partials;
+    args.sk_flags = sk_flags;
     return dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
 }
 
@@ -774,6 +850,31 @@ void vg_shard_rows(long long M, int world, int rank, long long *row0, long long 
         *rows = n;
 }
 
+int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, int group_m,
+                  int num_kb, int *out, int max_units) {
+    if (worker < 0 || workers <= 0 || worker >= workers || num_m <= 0 || num_n <= 0 ||
+        group_m <= 0 || num_kb <= 0 || max_units < 0)
+        return -1;
+    vg::UnitIter it;
+    it.init(stream_k != 0, worker, workers, num_m, num_n, group_m, num_kb);
+    vg::WorkUnit u;
+    int n = 0;
+    while (it.next(u)) {
+        if (out && n < max_units) {
+            int *o = out + 7 * n;
+            o[0] = u.tile_m;
+            o[1] = u.tile_n;
+            o[2] = u.kb0;
+            o[3] = u.kb1;
+            o[4] = u.kind;
+            o[5] = u.first_contrib;
+            o[6] = u.last_contrib;
+        }
+        ++n;
+    }
+    return n;
+}
+
 void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *tile_n) {
     int tm = -1, tn = -1;
     if (num_m > 0 && num_n > 0 && group_m > 0 && t >= 0 && t < num_m * num_n)
@@ -790,9 +891,9 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
     const int e = vg::make_plan(version, M, N, K, A, B, C, f32_out != 0, num_sms, num_sms / 2, p);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[14] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
+    const int vals[15] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
                           p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
-                          p.grid,      p.persistent,  p.bn,          p.version};
+                          p.grid,      p.persistent,  p.bn,          p.version, p.stream_k};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }
