@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol(vg):
 
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
-                             "VibeGEMM B200 v3", "VibeGEMM B200 v4"]
+                             "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -82,8 +82,8 @@ def test_plan_aligned_square(vg):
     ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 3), ((4096, 14336, 4096), 3),
     ((4096, 4096, 14336), 3), ((8191, 8193, 4099), 3),
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
-    ((1000, 3000, 2048), 4),     # fewer pair tiles than pair slots: stream-K
-    ((512, 512, 512), 1),
+    ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
+    ((512, 512, 512), 5),
 ])
 def test_auto_version_choice(vg, shape, want):
     assert vg.plan(-1, *shape, 256, 256, 256)["version"] == want

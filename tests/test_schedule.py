@@ -54,9 +54,10 @@ def test_stream_k_partition_and_owners(vg, num_m, num_n, kb, workers):
         assert first == w + 1
 
 
-def test_auto_picks_stream_k_for_underfilled_grids(vg):
-    p = vg.plan(-1, 1000, 3000, 2048, 256, 256, 256)
-    assert p["version"] == 4 and p["stream_k"] == 1
-    assert p["grid"] == 148  # 74 pairs, 1536 iterations
-    assert vg.plan(-1, 512, 512, 512, 256, 256, 256)["version"] == 1  # too few iterations
-    assert vg.plan(-1, 8192, 8192, 8192, 256, 256, 256)["stream_k"] == 0
+def test_stream_k_plan(vg):
+    p = vg.plan(4, 1000, 3000, 2048, 256, 256, 256)
+    assert p["stream_k"] == 1 and p["grid"] == 148  # 74 pairs, 1536 iterations
+    assert vg.plan(4, 256, 256, 64, 256, 256, 256)["grid"] == 2  # 1 tile x 1 k-block: one worker
+    # the per-shape choice never uses stream-K
+    for shape in [(1000, 3000, 2048), (512, 512, 512), (8192, 8192, 8192), (2048, 2048, 8192)]:
+        assert vg.plan(-1, *shape, 256, 256, 256)["stream_k"] == 0

@@ -196,7 +196,10 @@ class HostPipeline:
 
     Owns the device buffers (grown on demand) and the C pipeline (three streams). Each
     call enqueues the work and makes `stream` (default: current) wait for the result;
-    synchronise that stream before reading `out`.
+    synchronise that stream before reading `out`. The copies run after the call returns,
+    so the wrapper keeps every call's host tensors alive until an event recorded on
+    `stream` after the call has completed (torch would otherwise recycle a freed pinned
+    block while the library's upload still reads it).
     """
 
     def __init__(self, device: Optional[int] = None, chunks: int = 4):
@@ -207,6 +210,7 @@ class HostPipeline:
         if not self._h:
             raise VibeGemmError("vg_host_pipeline_create", -1)
         self._bufs = {}
+        self._in_flight = []  # (event, host tensors) of calls that may still be copying
 
     def _buf(self, name, shape):
         import torch
@@ -224,10 +228,15 @@ class HostPipeline:
         if not (A.is_pinned() and B.is_pinned() and out.is_pinned()):
             raise ValueError("host tensors must be pinned (pin_memory=True)")
         dA, dB, dC = self._buf("A", (M, K)), self._buf("B", (N, K)), self._buf("C", (M, N))
+        import torch
+        self._in_flight = [(ev, keep) for ev, keep in self._in_flight if not ev.query()]
         code = lib().vg_host_pipeline_gemm_f16(self._h, A.data_ptr(), B.data_ptr(), out.data_ptr(),
                                                dA.data_ptr(), dB.data_ptr(), dC.data_ptr(),
                                                M, N, K, self.chunks, _stream_handle(stream))
         _check(code, "vg_host_pipeline_gemm_f16")
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream() if stream is None else stream)
+        self._in_flight.append((ev, (A, B, out)))
         return out
 
     def close(self):

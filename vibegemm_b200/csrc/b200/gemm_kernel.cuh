@@ -76,18 +76,19 @@ struct GemmArgs {
     // kEpiTmaF16Peers: peer GPUs' copies of this shard's rows (row 0 of the shard, ld = ldc).
     void *peers[kMaxPeers];
     int num_peers;
-    // Stream-K: per-(worker, CTA rank) fp32 partial slots (128 × BN floats each, in TMEM
-    // lane order) and ready flags (zeroed before the launch).
+    // Stream-K: per-(worker, CTA rank) fp32 partial slots (128 × BN floats each, column-quad
+    // major) and ready flags (zeroed before the launch).
     float *sk_partials;
     unsigned *sk_flags;
 };
 
 template <int CG, int BN_> struct TileCfg {
-    static_assert(BN_ == 256 || (BN_ == 512 && CG == 2), "tile: 128x256, pair 256x256 or 256x512");
+    static_assert(BN_ == 256 || (BN_ == 192 && CG == 1) || (BN_ == 512 && CG == 2),
+                  "tile: 128x256, 128x192, pair 256x256 or pair 256x512");
     static constexpr int BM = 128;          // accumulator rows per CTA (TMEM lanes)
     static constexpr int BN = BN_;          // tile columns
     static constexpr int BK = 64;           // fp16 per 128-B swizzle row
-    static constexpr int NSUB = BN / 256;   // N=256 MMAs per K step
+    static constexpr int NSUB = BN > 256 ? BN / 256 : 1; // MMAs per K step (N <= 256 each)
     static constexpr int ACC_BUFS = (NSUB == 1) ? 2 : 1;
     static constexpr int B_ROWS = BN / CG;  // rows of B each CTA loads (one TMA box, <= 256)
     static constexpr int A_BYTES = BM * BK * 2;
@@ -95,7 +96,7 @@ template <int CG, int BN_> struct TileCfg {
     static constexpr int B_SUB_BYTES = B_BYTES / NSUB; // this CTA's B rows feeding one MMA
     static constexpr int STAGE_TX = CG * (A_BYTES + B_BYTES); // bytes landing per stage
     static constexpr int TMEM_COLS = 512;
-    static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, 256);
+    static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, BN / NSUB);
     static constexpr int EPI_WARPS = 4;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int STG_BYTES = 32 * 128; // one 32-row × 64-col fp16 box
@@ -466,7 +467,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                 args.num_kb);
         WorkUnit u;
-        // Stream-K partial slot of (worker, CTA rank), TMEM lane order: [BN/32][128][32] floats.
+        // Stream-K partial slot of (worker, CTA rank): 128 × BN floats.
         auto slot_of = [&](int worker) {
             return args.sk_partials + static_cast<long long>(worker * CG + static_cast<int>(rank)) *
                                           (T::BM * T::BN);
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 ptx::tmem_wait_ld();
                 // Last read of a release unit (a whole buffer, or one half of the BN=512
                 // accumulator): hand those TMEM columns back to the MMA issuer.
-                if (c % 4 == 3) {
+                if ((T::ACC_BUFS == 2) ? (c == T::BN / 64 - 1) : (c % 4 == 3)) {
                     const int unit = (T::ACC_BUFS == 2) ? acc : (c >> 2);
                     ptx::tc_fence_before();
                     __syncwarp();
@@ -508,26 +509,29 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 }
                 const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
                 if constexpr (SK) {
-                    const long long lane_off = (static_cast<long long>(sub) * 32 + lane) * 32;
+                    // Partial slot layout [BN/4 column quads][128 rows][4 floats]: for a
+                    // fixed quad the 32 lanes (32 consecutive rows) touch 512 contiguous
+                    // bytes, so every partial store / load is one coalesced warp access.
+                    const long long row_off = (static_cast<long long>(sub) * 32 + lane) * 4;
+                    const long long quad0 = static_cast<long long>(c) * 16; // 64 cols = 16 quads
                     if (u.kind == kUnitPartial) {
-                        // Park the fp32 accumulator: each lane writes its row's 2 × 32 floats,
-                        // a warp 2 × 4 KB contiguous.
-                        float *dst = slot_of(it.w) + static_cast<long long>(2 * c) * (T::BM * 32) + lane_off;
+                        float *dst = slot_of(it.w) + row_off;
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
-                            reinterpret_cast<uint4 *>(dst)[q] = make_uint4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
-                            reinterpret_cast<uint4 *>(dst + T::BM * 32)[q] =
+                            *reinterpret_cast<uint4 *>(dst + (quad0 + q) * (T::BM * 4)) =
+                                make_uint4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
+                            *reinterpret_cast<uint4 *>(dst + (quad0 + 8 + q) * (T::BM * 4)) =
                                 make_uint4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]);
                         }
                         continue;
                     }
                     if (u.kind == kUnitOwner && epi_ok) {
                         for (int w2 = u.first_contrib; w2 <= u.last_contrib; ++w2) {
-                            const float *src = slot_of(w2) + static_cast<long long>(2 * c) * (T::BM * 32) + lane_off;
+                            const float *src = slot_of(w2) + row_off;
 #pragma unroll
                             for (int q = 0; q < 8; ++q) {
-                                const float4 a = reinterpret_cast<const float4 *>(src)[q];
-                                const float4 b = reinterpret_cast<const float4 *>(src + T::BM * 32)[q];
+                                const float4 a = *reinterpret_cast<const float4 *>(src + (quad0 + q) * (T::BM * 4));
+                                const float4 b = *reinterpret_cast<const float4 *>(src + (quad0 + 8 + q) * (T::BM * 4));
                                 v0[4 * q] = __float_as_uint(__uint_as_float(v0[4 * q]) + a.x);
                                 v0[4 * q + 1] = __float_as_uint(__uint_as_float(v0[4 * q + 1]) + a.y);
                                 v0[4 * q + 2] = __float_as_uint(__uint_as_float(v0[4 * q + 2]) + a.z);

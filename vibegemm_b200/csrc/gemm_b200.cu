@@ -17,6 +17,8 @@
 //       are split evenly over the co-resident pairs; split tiles are finished by the
 //       pair holding k-block 0 from fp32 partials in a workspace. For grids with fewer
 //       tiles than pair slots.
+//   v5  v1 with 128×192 tiles (UMMA N=192): for grids too small to fill the GPU with
+//       128×256 tiles, a third more tiles of three quarters the work.
 //   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
@@ -59,6 +61,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v2", 2, 256, 6, true, true, 8},
     {"VibeGEMM B200 v3", 2, 512, 4, true, true, 16},
     {"VibeGEMM B200 v4", 2, 256, 6, true, true, 8, true},
+    {"VibeGEMM B200 v5", 1, 192, 4, true, true, 8},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -68,20 +71,28 @@ constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's 
 // full wave of pair tiles; short K (< 1024) favours the double-buffered 256×256 pair
 // (v2), whose epilogue fully overlaps the next tile; grids too small to fill the
 // pairs favour 128×256 single-CTA tiles (v1), which occupy twice as many SMs.
-// Grids with fewer 256×256 tiles than pair slots but enough k-blocks to give every pair
-// at least 4 go to stream-K (v4), which keeps all pairs busy.
+// Grids with fewer 256×256 tiles than pair slots cannot fill the GPU with one wave of
+// pairs; among the 256×256 pair (v2), 128×256 (v1) and 128×192 (v5) tiles pick the least
+// estimated time, waves × tile width / relative per-SM efficiency (pairs 1.1, 128×256 1.0,
+// 128×192 0.95: measured on the BASELINE shapes). Stream-K (v4) is never chosen: on B200
+// its fp32 fix-up traffic (128 KB per split tile and CTA) costs more than the idle SMs it
+// recovers on these sizes (measured with per-unit timestamps).
 int select_version(int M, int N, int K, int num_sms) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
-    const long long kb = ceil_div_i(K, 64);
     if (K >= 1024 && t3 >= pairs)
         return 3;
     if (t2 >= pairs)
         return 2;
-    if (t2 * kb >= 4 * pairs)
-        return 4;
-    return 1;
+    const long long t1 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 256);
+    const long long t5 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 192);
+    const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 / 1.1;
+    const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 / 1.0;
+    const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 / 0.95;
+    if (e5 < e1 && e5 < e2)
+        return 5;
+    return e2 <= e1 ? 2 : 1;
 }
 
 constexpr int kMinSkIters = 4; // k-blocks per stream-K worker at least
@@ -289,6 +300,34 @@ bool get_map(CUtensorMap &out, const void *base, uint64_t cols, uint64_t rows, u
     return true;
 }
 
+// ── workspace pool ───────────────────────────────────────────────────────────
+// Per-call workspaces (pad copies, stream-K partials) come from a stream-ordered pool
+// owned by the library, one per device, that keeps its memory across synchronisations
+// (release threshold = max) so repeated calls never go back to the driver.
+cudaMemPool_t g_pool[kMaxDevices];
+cudaError_t g_pool_err[kMaxDevices];
+std::once_flag g_pool_once[kMaxDevices];
+
+cudaError_t workspace_pool(int dev, cudaMemPool_t &pool) {
+    std::call_once(g_pool_once[dev], [dev] {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaError_t e = cudaMemPoolCreate(&g_pool[dev], &props);
+        if (e == cudaSuccess) {
+            uint64_t keep = ~0ull;
+            e = cudaMemPoolSetAttribute(g_pool[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+        if (e != cudaSuccess)
+            (void)cudaGetLastError();
+        g_pool_err[dev] = e;
+    });
+    pool = g_pool[dev];
+    return g_pool_err[dev];
+}
+
 // ── pad pre-pass ─────────────────────────────────────────────────────────────
 // dst[r, 0:ld_dst] = src[r, 0:cols] followed by zeros; ld_dst % 8 == 0, dst 16-B
 // aligned. One thread writes one 16-B group; reads are coalesced 2-B loads (src
@@ -429,6 +468,8 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
                      const GemmArgs *args, int grid, cudaStream_t s) {
     if (p.cta_group == 1 && p.bn == 256 && p.stages == 4)
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    if (p.cta_group == 1 && p.bn == 192 && p.stages == 4)
+        return dispatch_epi<1, 192, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 2 && p.bn == 512 && p.stages == 4)
@@ -513,7 +554,10 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     float *sk_partials = nullptr;
     unsigned *sk_flags = nullptr;
     if (wl.total) {
-        e = cudaMallocAsync(&ws, wl.total, s);
+        cudaMemPool_t pool;
+        e = workspace_pool(dev, pool);
+        if (e == cudaSuccess)
+            e = cudaMallocFromPoolAsync(&ws, wl.total, pool, s);
         if (e != cudaSuccess)
             return e;
         char *base = static_cast<char *>(ws);

@@ -43,6 +43,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v4 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<4>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v4
+namespace gemm_b200_v5 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<5>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v5
 // The default entry point: one of the versions above, chosen per shape.
 namespace gemm_b200_auto {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
@@ -76,4 +79,5 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v1", GeneratedB200KernelBackend<gemm_b200_v1
 REGISTER_B200_KERNEL("VibeGEMM B200 v2", GeneratedB200KernelBackend<gemm_b200_v2::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v3", GeneratedB200KernelBackend<gemm_b200_v3::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v4", GeneratedB200KernelBackend<gemm_b200_v4::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v5", GeneratedB200KernelBackend<gemm_b200_v5::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
