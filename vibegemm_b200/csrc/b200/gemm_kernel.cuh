@@ -96,6 +96,7 @@ template <int CG, int BN_> struct TileCfg {
     static constexpr int B_SUB_BYTES = B_BYTES / NSUB; // this CTA's B rows feeding one MMA
     static constexpr int STAGE_TX = CG * (A_BYTES + B_BYTES); // bytes landing per stage
     static constexpr int TMEM_COLS = 512;
+    static constexpr int ACC_STRIDE = 256; // TMEM columns between the two accumulator buffers
     static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, BN / NSUB);
     static constexpr int EPI_WARPS = 4;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         break;
                     }
                     ptx::tc_fence_after();
-                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::BN);
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::ACC_STRIDE);
                     for (int kb = 0; kb < nkb; ++kb) {
                         if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                             ok = false;
@@ -487,7 +488,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 __syncwarp();
             }
             const uint32_t t_row =
-                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * 256);
+                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
 #pragma unroll 1
             for (int c = 0; c < T::BN / 64; ++c) {
                 uint32_t v0[32], v1[32];
