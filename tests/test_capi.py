@@ -95,7 +95,7 @@ def test_plan_tails_and_alignment(vg):
     # N*2 not a multiple of 16 -> direct-store epilogue.
     p = vg.plan(2, 8191, 8193, 4099, 256, 256, 256)
     assert (p["pad_a"], p["pad_b"], p["k_padded"]) == (1, 1, 4104)
-    assert p["epilogue"] == "direct_f16"
+    assert p["epilogue"] == "staged_f16"
     assert (p["num_m_tiles"], p["num_n_tiles"], p["num_kb"]) == (32, 33, 65)
     # 1000x3000x2048: aligned strides, partial tiles, under-filled grid.
     p = vg.plan(2, 1000, 3000, 2048, 256, 256, 256)
@@ -105,7 +105,8 @@ def test_plan_tails_and_alignment(vg):
     p = vg.plan(2, 512, 512, 512, 258, 256, 256)
     assert (p["pad_a"], p["pad_b"]) == (1, 0)
     # A misaligned C pointer switches to direct stores; fp32 output always direct.
-    assert vg.plan(2, 512, 512, 512, 256, 256, 258)["epilogue"] == "direct_f16"
+    assert vg.plan(2, 512, 512, 512, 256, 256, 258)["epilogue"] == "staged_f16"
+    assert vg.plan(0, 512, 512, 512, 256, 256, 258)["epilogue"] == "direct_f16"
     assert vg.plan(2, 512, 512, 512, 256, 256, 256, f32_out=True)["epilogue"] == "direct_f32"
 
 

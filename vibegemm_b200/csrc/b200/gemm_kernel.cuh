@@ -48,6 +48,7 @@ enum EpiKind : int {
     kEpiDirectF16 = 1, // predicated global stores (any C alignment / ldc)
     kEpiDirectF32 = 2, // fp32 output, validation build of the same main loop
     kEpiTmaF16Peers = 3, // TMA store to local C + the same rows into every peer GPU's C
+    kEpiStagedF16 = 4,   // smem staging + row-cooperative coalesced stores (any C alignment)
 };
 
 constexpr int kMaxPeers = 7; // peers of one node (8 GPUs per NVSwitch domain)
@@ -118,8 +119,9 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
     static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
-    static constexpr int EPI_BYTES =
-        (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) ? T::EPI_WARPS * 2 * T::STG_BYTES : 0;
+    static constexpr int EPI_BYTES = (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers || EPI == kEpiStagedF16)
+                                         ? T::EPI_WARPS * 2 * T::STG_BYTES
+                                         : 0;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
     static constexpr int SLOT_OFF = BAR_OFF + 8 * NUM_BARS;
@@ -545,7 +547,48 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         }
                     }
                 }
-                if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
+                if constexpr (EPI == kEpiStagedF16) {
+                    // C rows are not 16-B aligned (N % 8 != 0 or an offset base): stage the
+                    // 32 × 64 box, then write it row by row, 32 lanes covering 64 contiguous
+                    // bytes per store instruction.
+                    uint32_t p[32];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
+                        p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
+                    }
+                    const uint32_t stg = sEpi + static_cast<uint32_t>(ew * 2 * T::STG_BYTES);
+                    __syncwarp(); // previous chunk's reads of this buffer are done
+                    const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                                     "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
+                                     "r"(p[4 * j + 3])
+                                     : "memory");
+                    }
+                    __syncwarp();
+                    __half *cbase = static_cast<__half *>(args.C);
+#pragma unroll 4
+                    for (int r = 0; r < 32; ++r) {
+                        const int grow = row0 + r;
+                        if (grow >= args.M)
+                            break;
+                        __half *crow = cbase + static_cast<long long>(grow) * args.ldc;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int col = h * 32 + lane; // column within the box
+                            const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
+                                               (static_cast<uint32_t>((col >> 3) ^ (r & 7)) << 4) +
+                                               static_cast<uint32_t>(col & 7) * 2u;
+                            unsigned short bits;
+                            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(a));
+                            if (ccol + col < args.N)
+                                reinterpret_cast<unsigned short *>(crow)[ccol + col] = bits;
+                        }
+                    }
+                } else if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
                     uint32_t p[32];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {

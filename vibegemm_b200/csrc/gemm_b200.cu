@@ -24,8 +24,8 @@
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
 // strides: when A or B (K % 8 != 0 or a misaligned pointer) cannot be described,
 // a pre-pass copies it into a K-padded workspace from the stream-ordered pool;
-// when C cannot be (N % 8 != 0 or misaligned), the epilogue switches to predicated
-// direct stores. Partial tiles use TMA out-of-bounds zero fill and store clipping.
+// when C cannot be (N % 8 != 0 or misaligned), the epilogue stages each box in shared
+// memory and writes it row by row with coalesced 2-B stores. Partial tiles use TMA out-of-bounds zero fill and store clipping.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -160,6 +160,8 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
         p.epi = kEpiDirectF32;
     else if (v.tma_store && N % 8 == 0 && aligned16(C))
         p.epi = kEpiTmaF16;
+    else if (v.tma_store)
+        p.epi = kEpiStagedF16; // C rows TMA cannot describe: staged, coalesced row stores
     else
         p.epi = kEpiDirectF16;
     p.num_m_tiles = ceil_div_i(M, 128 * v.cta_group);
@@ -447,6 +449,7 @@ cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
             VG_EPI_CASE(kEpiTmaF16)
             VG_EPI_CASE(kEpiDirectF16)
             VG_EPI_CASE(kEpiDirectF32)
+            VG_EPI_CASE(kEpiStagedF16)
         default:
             return cudaErrorInvalidValue;
         }
@@ -456,6 +459,7 @@ cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
             VG_EPI_CASE(kEpiDirectF16)
             VG_EPI_CASE(kEpiDirectF32)
             VG_EPI_CASE(kEpiTmaF16Peers)
+            VG_EPI_CASE(kEpiStagedF16)
         default:
             return cudaErrorInvalidValue;
         }
