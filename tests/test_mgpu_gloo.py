@@ -77,3 +77,52 @@ def test_shard_rows_python_matches_c_abi(vg):
         for world in (1, 2, 3, 4, 8):
             for r in range(world):
                 assert shard_rows(M, world, r) == vg.shard_rows(M, world, r)
+
+
+def _leaver(rank, world, port, q):
+    """Rank 1 joins the group, then leaves before the all-gather of C; rank 0 must get an
+    error from its collective within the process-group timeout instead of hanging."""
+    import sys
+    import time
+    from datetime import timedelta
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import torch
+    import torch.distributed as dist
+    from vibegemm_b200.mgpu import RowShardedGemm
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # flush the message before the abrupt exit
+        os._exit(0)  # leaves between steps: no collective of its own is in flight
+    sh = RowShardedGemm(64, 16, 8, rank, world)
+    C_loc = torch.zeros((sh.local[1], 16), dtype=torch.float16)
+    t0 = time.time()
+    try:
+        sh.gather(C_loc)
+        q.put((rank, "no error"))
+    except Exception as e:  # the surviving rank learns of the failure from the collective
+        q.put((rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_is_detected_by_timeout():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = dict(q.get(timeout=10) for _ in range(2))
+    assert out[1] == "left"
+    assert out[0].startswith("error after"), out[0]
