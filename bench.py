@@ -64,9 +64,10 @@ def parse_args():
     ap.add_argument("--version", type=int, default=None, help="kernel version (default: the per-shape choice of vg_b200_gemm_f16)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    ap.add_argument("--allgather", choices=["none", "nccl", "fused"], default="none",
+    ap.add_argument("--allgather", choices=["none", "nccl", "fused", "fused-p2p"], default="none",
                     help="N>1: also time the all-gather of C, as a separate NCCL all-gather after "
-                         "the GEMM (nccl) or fused into the GEMM kernel's epilogue over NVLink (fused)")
+                         "the GEMM (nccl) or fused into the GEMM kernel's epilogue over NVLink "
+                         "(fused: NVLink multicast when available; fused-p2p: one store per peer)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm8192")
     return ap.parse_args()
 
@@ -344,9 +345,9 @@ def run_b200(args) -> None:
         allgather = {"mode": "nccl", "ms_per_step": ms_ag, "bytes_gathered": M * N_DIM * 2,
                      "gemm_plus_allgather_value": flop_step / ((ms + ms_ag) * 1e-3) / 1e12,
                      "note": "NCCL all_gather_into_tensor of the row-major C shards, timed after the GEMM"}
-    elif args.allgather == "fused" and world > 1:
+    elif args.allgather in ("fused", "fused-p2p") and world > 1:
         from vibegemm_b200.mgpu import FusedAllGatherGemm
-        fused = FusedAllGatherGemm(M, N_DIM, K_DIM, rank, world)
+        fused = FusedAllGatherGemm(M, N_DIM, K_DIM, rank, world, multicast=args.allgather == "fused")
 
         def fused_step():
             fused.run(A, B, stream=stream)
@@ -363,7 +364,8 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
         ok_rows = bool(torch.equal(fused.C[p0:p0 + prow], want))
         ok_all = max_over_ranks(0.0 if ok_rows else 1.0) == 0.0
-        allgather = {"mode": "fused", "ms_per_step": ms_fused, "bytes_gathered": M * N_DIM * 2,
+        allgather = {"mode": "fused-multicast" if fused.c_multicast_ptr else "fused-p2p",
+                     "ms_per_step": ms_fused, "bytes_gathered": M * N_DIM * 2,
                      "gemm_plus_allgather_value": flop_step / (ms_fused * 1e-3) / 1e12,
                      "gathered_rows_exact": ok_all,
                      "note": "one kernel per rank: the epilogue stores each C tile into every "

@@ -135,13 +135,15 @@ int vg_b200_selftest_wait_timeout(unsigned long long timeout_ns);
  * and the replicated B, and its epilogue writes every finished C tile both into its own
  * full-size C (C_ranks[rank]) and, over NVLink, into every other rank's full-size C:
  * C_ranks[r] must be rank r's M×N C buffer mapped into this process (peer pointers, e.g.
- * from symmetric memory), N % 8 == 0 and 16-B aligned rows. The all-gather's traffic
- * overlaps the math tile by tile. No kernel waits on another GPU: after the call, the
- * ranks must synchronise (e.g. a barrier) before reading rows written by peers.
- * Returns 0 or a cudaError_t code. */
-int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks, int world,
-                               int rank, long long row0, int M_local, int N, int K,
-                               vg_stream_t stream);
+ * from symmetric memory), N % 8 == 0 and 16-B aligned rows. If C_multicast is not NULL it
+ * is the NVLink-multicast (NVLS) address of the same M×N buffers: each tile is then sent
+ * once with multimem stores and the switch delivers it to every rank; otherwise one store
+ * per peer. The all-gather's traffic overlaps the math tile by tile. No kernel waits on
+ * another GPU: after the call, the ranks must synchronise (e.g. a barrier) before reading
+ * rows written by peers. Returns 0 or a cudaError_t code. */
+int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks,
+                               void *C_multicast, int world, int rank, long long row0, int M_local,
+                               int N, int K, vg_stream_t stream);
 
 /* Contiguous row-block sharding used by the multi-GPU driver (A and C split by rows,
  * B replicated): rank r of `world` owns rows [row0, row0 + rows). No reference

@@ -1,8 +1,9 @@
 """Fused row-sharded GEMM + all-gather of C on 2 GPUs (skipped with fewer GPUs).
 
 Each rank computes its row block of C with vg_b200_gemm_f16_allgather, whose epilogue also
-writes the rows into the other rank's full C over NVLink; after a barrier every rank's full
-C must equal a single-GPU GEMM of the whole problem, bit for bit.
+writes the rows into the other rank's full C over NVLink — one store per peer, or one
+NVLink-multicast (multimem) store when the node supports NVLS; after a barrier every rank's
+full C must equal a single-GPU GEMM of the whole problem, bit for bit.
 """
 import os
 import socket
@@ -19,7 +20,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, N, K, q):
+def _worker(rank, world, port, M, N, K, multicast, q):
     import sys
     from datetime import timedelta
     from pathlib import Path
@@ -36,7 +37,7 @@ def _worker(rank, world, port, M, N, K, q):
                             device_id=torch.device("cuda", rank))
     try:
         A, B = oracle.make_inputs(M, N, K)
-        fused = FusedAllGatherGemm(M, N, K, rank, world)
+        fused = FusedAllGatherGemm(M, N, K, rank, world, multicast=multicast)
         r0, rows = fused.sh.local
         dA = torch.from_numpy(A[r0:r0 + rows].view(np.int16).copy()).cuda().view(torch.float16)
         dB = torch.from_numpy(B.view(np.int16).copy()).cuda().view(torch.float16)
@@ -45,15 +46,16 @@ def _worker(rank, world, port, M, N, K, q):
         fused.barrier()
         full = vg.gemm(torch.from_numpy(A.view(np.int16).copy()).cuda().view(torch.float16), dB)
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(fused.C, full)), vg.device_status()))
+        q.put((rank, bool(torch.equal(fused.C, full)), vg.device_status(), bool(fused.c_multicast_ptr)))
         fused.barrier()
         del fused
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("multicast", [False, True], ids=["p2p", "nvls"])
 @pytest.mark.parametrize("M,N,K", [(1536, 2048, 1024), (1001, 1024, 4099)])
-def test_fused_gemm_allgather_two_gpus(M, N, K):
+def test_fused_gemm_allgather_two_gpus(M, N, K, multicast):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -62,7 +64,7 @@ def test_fused_gemm_allgather_two_gpus(M, N, K):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, multicast, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -74,3 +76,5 @@ def test_fused_gemm_allgather_two_gpus(M, N, K):
     res = sorted(q.get(timeout=10) for _ in range(world))
     assert [r[1] for r in res] == [True, True], res
     assert [r[2] for r in res] == [0, 0], res
+    if multicast and not res[0][3]:
+        pytest.skip("no NVLink multicast on this node (per-peer path was checked)")

@@ -43,9 +43,10 @@ _SIGS = {
     "vg_b200_plan": (ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.c_size_t] * 3 + [ctypes.c_int] * 2
                      + [ctypes.POINTER(ctypes.c_int)]),
     "vg_b200_gemm_f16_allgather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
-                                                   ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
-                                                   ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
-                                                   ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+                                                   ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_longlong,
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.c_void_p]),
     "vg_host_pipeline_create": (ctypes.c_void_p, [ctypes.c_int]),
     "vg_host_pipeline_destroy": (None, [ctypes.c_void_p]),
     "vg_host_pipeline_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 7 + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
@@ -176,18 +177,21 @@ def cublas_gemm(A, B, out=None, stream=None):
 AUTO = -1  # per-shape version choice (the default entry point's policy)
 
 
-def gemm_allgather(A_local, B, c_rank_ptrs, rank: int, row0: int, stream=None) -> None:
+def gemm_allgather(A_local, B, c_rank_ptrs, rank: int, row0: int, stream=None,
+                   c_multicast_ptr: int = 0) -> None:
     """Fused row-sharded GEMM + all-gather: writes C rows [row0, row0+M_local) into every
-    rank's full C (`c_rank_ptrs[r]`, device pointers valid in this process). Barrier across
-    ranks before reading rows written by peers."""
+    rank's full C (`c_rank_ptrs[r]`, device pointers valid in this process; with
+    `c_multicast_ptr` through NVLink multicast instead). Barrier across ranks before reading
+    rows written by peers."""
     import torch
     if not (A_local.is_cuda and B.is_cuda) or A_local.dtype != torch.float16 or B.dtype != torch.float16:
         raise ValueError("A_local and B must be float16 CUDA tensors")
     M_local, K = A_local.shape
     N = B.shape[0]
     arr = (ctypes.c_void_p * len(c_rank_ptrs))(*c_rank_ptrs)
-    code = lib().vg_b200_gemm_f16_allgather(A_local.data_ptr(), B.data_ptr(), arr, len(c_rank_ptrs),
-                                            rank, row0, M_local, N, K, _stream_handle(stream))
+    code = lib().vg_b200_gemm_f16_allgather(A_local.data_ptr(), B.data_ptr(), arr,
+                                            c_multicast_ptr or None, len(c_rank_ptrs), rank, row0,
+                                            M_local, N, K, _stream_handle(stream))
     _check(code, "vg_b200_gemm_f16_allgather")
 
 

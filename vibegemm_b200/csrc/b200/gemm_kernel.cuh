@@ -74,9 +74,12 @@ struct GemmArgs {
     void *C;         // direct epilogues only
     long long ldc;   // elements
     unsigned long long timeout_ns;
-    // kEpiTmaF16Peers: peer GPUs' copies of this shard's rows (row 0 of the shard, ld = ldc).
+    // kEpiTmaF16Peers: peer GPUs' copies of this shard's rows (row 0 of the shard, ld = ldc),
+    // or, when `mc` is set, the NVLink-multicast address of that row in every rank's C: one
+    // multimem store reaches all ranks through the switch.
     void *peers[kMaxPeers];
     int num_peers;
+    void *mc;
     // Stream-K: per-(worker, CTA rank) fp32 partial slots (128 × BN floats each, column-quad
     // major) and ready flags (zeroed before the launch).
     float *sk_partials;
@@ -633,8 +636,15 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             const int gcol = ccol + 8 * j;
                             if (grow < args.M && gcol < args.N) {
                                 const long long off = static_cast<long long>(grow) * args.ldc + gcol;
-                                for (int pr = 0; pr < args.num_peers; ++pr)
-                                    *reinterpret_cast<uint4 *>(static_cast<__half *>(args.peers[pr]) + off) = q;
+                                if (args.mc) {
+                                    const __half *dst = static_cast<__half *>(args.mc) + off;
+                                    asm volatile("multimem.st.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                                                 "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w)
+                                                 : "memory");
+                                } else {
+                                    for (int pr = 0; pr < args.num_peers; ++pr)
+                                        *reinterpret_cast<uint4 *>(static_cast<__half *>(args.peers[pr]) + off) = q;
+                                }
                             }
                         }
                     }

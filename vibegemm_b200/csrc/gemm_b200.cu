@@ -506,7 +506,8 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 }
 
 cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
-                     bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0) {
+                     bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0,
+                     void *mc = nullptr) {
     if ((version != kAutoVersion && (version < 0 || version >= kNumVersions)) || M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
@@ -534,6 +535,8 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     for (int i = 0; i < num_peers; ++i)
         if (!peers || !peers[i] || !aligned16((uintptr_t)peers[i]))
             return cudaErrorInvalidValue;
+    if (mc && (num_peers == 0 || !aligned16((uintptr_t)mc)))
+        return cudaErrorInvalidValue;
     Plan p;
     e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, f32_out,
                                di->num_sms, di->num_sms / 2, p, num_peers > 0);
@@ -617,6 +620,7 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
+    args.mc = mc;
 
     e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
     if (ws) {
@@ -781,9 +785,9 @@ int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N
     return vg::run_gemm_noalloc(A, B, C, M, N, K, (cudaStream_t)stream);
 }
 
-int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks, int world,
-                               int rank, long long row0, int M_local, int N, int K,
-                               vg_stream_t stream) {
+int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks,
+                               void *C_multicast, int world, int rank, long long row0, int M_local,
+                               int N, int K, vg_stream_t stream) {
     if (!C_ranks || world < 1 || world > vg::kMaxPeers + 1 || rank < 0 || rank >= world || row0 < 0 ||
         M_local < 0 || N < 0)
         return (int)cudaErrorInvalidValue;
@@ -797,8 +801,9 @@ int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *
             peers[np++] = static_cast<char *>(C_ranks[r]) + off;
     }
     void *C_local = static_cast<char *>(C_ranks[rank]) + off;
+    void *mc = C_multicast ? static_cast<char *>(C_multicast) + off : nullptr;
     return (int)vg::run_gemm(vg::kAutoVersion, A_local, B, C_local, M_local, N, K, false,
-                             (cudaStream_t)stream, peers, np);
+                             (cudaStream_t)stream, peers, np, mc);
 }
 
 int vg_b200_num_versions(void) { return vg::kNumVersions; }

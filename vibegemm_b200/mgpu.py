@@ -78,7 +78,8 @@ class FusedAllGatherGemm:
     current stream; call ``barrier`` before reading rows written by other ranks.
     """
 
-    def __init__(self, M: int, N: int, K: int, rank: int, world: int, group=None):
+    def __init__(self, M: int, N: int, K: int, rank: int, world: int, group=None,
+                 multicast: bool = True):
         import torch
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
@@ -92,6 +93,9 @@ class FusedAllGatherGemm:
         base = self.handle.buffer_ptrs[rank]
         offset = self.C_full.data_ptr() - base
         self.c_rank_ptrs = [int(p) + offset for p in self.handle.buffer_ptrs]
+        # NVLink multicast (NVLS) address of the same buffers, when the node supports it.
+        mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
+        self.c_multicast_ptr = mc + offset if (multicast and mc) else 0
 
     @property
     def C(self):
@@ -101,7 +105,8 @@ class FusedAllGatherGemm:
         import vibegemm_b200 as vg
         r0, rows = self.sh.local
         if rows > 0:
-            vg.gemm_allgather(A_local, B, self.c_rank_ptrs, self.rank, r0, stream)
+            vg.gemm_allgather(A_local, B, self.c_rank_ptrs, self.rank, r0, stream,
+                              self.c_multicast_ptr)
 
     def barrier(self) -> None:
         import torch
