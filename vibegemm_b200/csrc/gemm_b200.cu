@@ -507,7 +507,7 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 
 cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
                      bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0,
-                     void *mc = nullptr) {
+                     void *c_multicast = nullptr) {
     if ((version != kAutoVersion && (version < 0 || version >= kNumVersions)) || M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
@@ -535,7 +535,7 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     for (int i = 0; i < num_peers; ++i)
         if (!peers || !peers[i] || !aligned16((uintptr_t)peers[i]))
             return cudaErrorInvalidValue;
-    if (mc && (num_peers == 0 || !aligned16((uintptr_t)mc)))
+    if (c_multicast && (num_peers == 0 || !aligned16((uintptr_t)c_multicast)))
         return cudaErrorInvalidValue;
     Plan p;
     e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, f32_out,
@@ -620,7 +620,7 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
-    args.mc = mc;
+    args.mc = c_multicast;
 
     e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
     if (ws) {
@@ -801,9 +801,9 @@ int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *
             peers[np++] = static_cast<char *>(C_ranks[r]) + off;
     }
     void *C_local = static_cast<char *>(C_ranks[rank]) + off;
-    void *mc = C_multicast ? static_cast<char *>(C_multicast) + off : nullptr;
+    void *c_mc = C_multicast ? static_cast<char *>(C_multicast) + off : nullptr;
     return (int)vg::run_gemm(vg::kAutoVersion, A_local, B, C_local, M_local, N, K, false,
-                             (cudaStream_t)stream, peers, np, mc);
+                             (cudaStream_t)stream, peers, np, c_mc);
 }
 
 int vg_b200_num_versions(void) { return vg::kNumVersions; }
