@@ -28,7 +28,8 @@ def test_library_exports_every_declared_symbol(vg):
 
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
-                             "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5"]
+                             "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
+                             "VibeGEMM B200 v6"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -79,7 +80,8 @@ def test_plan_aligned_square(vg):
 
 
 @pytest.mark.parametrize("shape,want", [
-    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 3), ((4096, 14336, 4096), 3),
+    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 6), ((4096, 14336, 4096), 3),
+    ((16384, 16384, 16384), 6), ((4096, 32768, 32768), 6),
     ((4096, 4096, 14336), 3), ((8191, 8193, 4099), 3),
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
     ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
