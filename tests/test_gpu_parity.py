@@ -157,3 +157,20 @@ def test_repeated_calls_deterministic(vg, orc):
         again = vg.gemm(dA, dB)
     torch.cuda.synchronize()
     assert torch.equal(first, again)
+
+
+def test_long_k_acceptance(vg, orc):
+    """K = 32768 (the sharded config's K): every version meets the BASELINE accumulation
+    bound on sampled rows of the fp32-output build, against the fp64 product."""
+    import torch
+    M, N, K = 256, 2048, 32768
+    A, B = orc.make_inputs(M, N, K)
+    rows = [0, 1, 130, 255]
+    exact = np.concatenate([orc.gemm_f64(A, B, r, 1) for r in rows])
+    dA, dB = to_dev(A), to_dev(B)
+    for v in VERSIONS:
+        C = vg.gemm_f32out(dA, dB, version=v)
+        torch.cuda.synchronize()
+        acc = orc.acceptance(C.cpu().numpy()[rows], exact, K=K)
+        assert acc["max_abs"] <= acc["abs_bound"], (v, acc)
+        assert acc["max_rel"] <= 1e-2, (v, acc)
