@@ -80,7 +80,8 @@ def test_plan_aligned_square(vg):
 
 
 @pytest.mark.parametrize("shape,want", [
-    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 6), ((4096, 14336, 4096), 3),
+    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 6),
+    ((4096, 14336, 4096), 2),    # 448 256x512 tiles = 6.05 waves; 896 256x256 tiles waste less
     ((16384, 16384, 16384), 6), ((4096, 32768, 32768), 6),
     ((4096, 4096, 14336), 3), ((8191, 8193, 4099), 3),
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator

@@ -89,8 +89,13 @@ int select_version(int M, int N, int K, int num_sms) {
     // 32768³ under the power cap, +0.6 % at 16384³; -0.5..-8 % at K <= 8192).
     if (K >= 16384 && t3 >= pairs)
         return 6;
-    if (K >= 1024 && t3 >= pairs)
-        return 3;
+    // Full waves of pair tiles: 256×512 (v3, ~6 % more work per pair-cycle than 256×256 at
+    // 8192³) against 256×256 (v2), each charged for its last partial wave.
+    if (K >= 1024 && t3 >= pairs) {
+        const double e3 = (double)((t3 + pairs - 1) / pairs) * 512 / 1.057;
+        const double e2 = (double)((t2 + pairs - 1) / pairs) * 256;
+        return e3 <= e2 ? 3 : 2;
+    }
     if (t2 >= pairs)
         return 2;
     const long long t1 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 256);
