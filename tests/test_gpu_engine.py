@@ -55,3 +55,25 @@ def test_bounded_wait_reports_timeout_instead_of_hanging(vg):
 
 def test_is_available_on_b200(vg):
     assert vg.is_available(0)
+
+
+@pytest.mark.gpu
+def test_driver_binary_logs_text_and_json(vg, tmp_path):
+    """The driver writes the reference's text log and one JSON line per backend; both parse."""
+    import json
+    import subprocess
+    from pathlib import Path
+
+    from vibegemm_b200 import perf_report
+
+    exe = Path(vg.__file__).resolve().parent / "bin" / "VibeGEMM"
+    proc = subprocess.run([str(exe), "512x512x512"], cwd=tmp_path, capture_output=True,
+                          text=True, timeout=300)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-2000:]
+    cublas, versions, tflops = perf_report.parse_perf_file(str(tmp_path / "results" / "perf_b200.txt"))
+    assert cublas > 0 and versions == [f"v{i}" for i in range(len(vg.versions()))]
+    assert all(t > 0 for t in tflops)
+    rows = [json.loads(line) for line in (tmp_path / "results" / "perf_b200.jsonl").read_text().splitlines()]
+    assert [r["backend"] for r in rows] == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
+    assert all(r["passed"] and (r["M"], r["N"], r["K"]) == (512, 512, 512) for r in rows)
+    assert rows[0]["pct_cublas"] == pytest.approx(100.0)

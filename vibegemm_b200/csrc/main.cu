@@ -7,12 +7,18 @@
 // results/perf_b200.txt. The default problem list is the reference's (8192³);
 // shapes can be given as arguments: `VibeGEMM [--normal] MxNxK ...`
 // (--normal = N(0, 0.02) inputs instead of uniform[-1,1]).
+// Besides the reference's text log, one JSON line per (backend, shape) goes to
+// results/perf_<arch>.jsonl: TFLOP/s, % of cuBLAS, % of the dense fp16 peak
+// (VG_PEAK_TFLOPS, else the nominal 2250 of B200), the check_error figures and the
+// host's core count.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
 #include <sys/stat.h>
+#include <thread>
 #include <vector>
 
 #include "engine.cuh"
@@ -30,6 +36,68 @@ static void log_print(const char *fmt, ...) {
         std::vfprintf(g_fp, fmt, args);
         va_end(args);
     }
+}
+
+static void json_string(FILE *fp, const std::string &v) {
+    std::fputc('"', fp);
+    for (char ch : v) {
+        if (ch == '"' || ch == '\\')
+            std::fputc('\\', fp);
+        if (static_cast<unsigned char>(ch) >= 0x20)
+            std::fputc(ch, fp);
+    }
+    std::fputc('"', fp);
+}
+
+// JSON has no inf / nan: non-finite error figures are written as null.
+static void json_number(FILE *fp, double v) {
+    if (std::isfinite(v))
+        std::fprintf(fp, "%.6g", v);
+    else
+        std::fputs("null", fp);
+}
+
+// One JSON object per backend result of the last engine.execute().
+static void write_json_results(FILE *fp, const cudaDeviceProp &prop, int sm, int M, int N, int K,
+                               bool normal, const std::vector<EngineResult> &results) {
+    double peak = 2250.0;
+    const char *peak_kind = "nominal";
+    if (const char *env = std::getenv("VG_PEAK_TFLOPS")) {
+        const double v = std::atof(env);
+        if (v > 0) {
+            peak = v;
+            peak_kind = "env";
+        }
+    }
+    double cublas = 0.0;
+    for (const auto &r : results)
+        if (r.ran && r.name.find("cuBLAS") != std::string::npos)
+            cublas = r.tflops;
+    for (const auto &r : results) {
+        std::fprintf(fp, "{\"gpu\": ");
+        json_string(fp, prop.name);
+        std::fprintf(fp, ", \"sm\": %d, \"ngpu\": 1, \"backend\": ", sm);
+        json_string(fp, r.name);
+        std::fprintf(fp, ", \"M\": %d, \"N\": %d, \"K\": %d, \"inputs\": \"%s\"", M, N, K,
+                     normal ? "normal(0,0.02)" : "uniform(-1,1)");
+        if (r.skipped || !r.ran) {
+            std::fprintf(fp, ", \"skipped\": %s, \"ran\": %s}\n", r.skipped ? "true" : "false",
+                         r.ran ? "true" : "false");
+            continue;
+        }
+        std::fprintf(fp,
+                     ", \"avg_ms\": %.6f, \"tflops\": %.2f, \"pct_cublas\": %.2f, \"pct_peak\": %.2f,"
+                     " \"peak_tflops\": %.1f, \"peak_kind\": \"%s\", \"max_abs_err\": ",
+                     r.avg_ms, r.tflops, cublas > 0 ? 100.0 * r.tflops / cublas : 0.0,
+                     100.0 * r.tflops / peak, peak, peak_kind);
+        json_number(fp, r.err.max_abs_err);
+        std::fprintf(fp, ", \"max_rel_err\": ");
+        json_number(fp, r.err.max_rel_err);
+        std::fprintf(fp, ", \"mismatches\": %zu, \"passed\": %s, \"cpu_cores\": %u}\n",
+                     r.err.mismatches, r.err.passed ? "true" : "false",
+                     std::thread::hardware_concurrency());
+    }
+    std::fflush(fp);
 }
 
 struct GemmProblem {
@@ -77,6 +145,12 @@ int main(int argc, char **argv) {
         return 1;
     }
     log_print("=== Device: %s (SM: %d) ===\n", prop.name, sm);
+    const std::string json_file = log_file.substr(0, log_file.size() - 4) + ".jsonl";
+    FILE *jfp = std::fopen(json_file.c_str(), "w");
+    if (!jfp) {
+        std::fprintf(stderr, "Failed to open %s for writing!\n", json_file.c_str());
+        return 1;
+    }
 
     BenchmarkEngine engine;
     engine.set_log_file(g_fp);
@@ -102,6 +176,7 @@ int main(int argc, char **argv) {
         if (c.label)
             log_print("\n>>> %s\n", c.label);
         engine.execute(c.m, c.n, c.k);
+        write_json_results(jfp, prop, sm, c.m, c.n, c.k, normal, engine.results());
         for (const auto &r : engine.results())
             if (!r.skipped && (!r.ran || !r.err.passed))
                 ++failures;
@@ -110,5 +185,6 @@ int main(int argc, char **argv) {
     std::fflush(g_fp);
     std::fclose(g_fp);
     g_fp = nullptr;
+    std::fclose(jfp);
     return failures == 0 ? 0 : 3;
 }
