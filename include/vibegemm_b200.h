@@ -98,6 +98,13 @@ int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C,
 int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
                        vg_stream_t stream);
 
+/* Validation twin of vg_cublas_gemm_f16 with fp32 C (cublasGemmEx, C type CUDA_R_32F,
+ * same compute type): cuBLAS's accumulation error next to vg_b200_gemm_f16_f32out's.
+ * No reference counterpart (the reference compares fp16 outputs only,
+ * include/utils.cuh:70-118). */
+int vg_cublas_gemm_f16_f32out(const void *A, const void *B, float *C, int M, int N, int K,
+                              vg_stream_t stream);
+
 /* Registry listing: replaces KernelRegistry::make_all / GemmBackend::name
  * (include/registry.cuh:23-32, include/backend.cuh:16). vg_b200_default_version() is -1
  * (per-shape choice); vg_b200_version_name(-1) is "VibeGEMM B200 auto". */

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(vg):
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
-                             "VibeGEMM B200 v6"]
+                             "VibeGEMM B200 v6", "VibeGEMM B200 v7"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -87,7 +87,11 @@ def test_plan_aligned_square(vg):
     ((8191, 8193, 4099), 2),     # 544 pair tiles of 256x512 = 7.4 waves; 1056 of 256x256 = 14.3
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
     ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
+    ((1000, 3000, 8192), 7),     # same tiles, long K: the fifth stage pays
     ((512, 512, 512), 5),
+    ((256, 2048, 32768), 4),     # 8 pair tiles, 512 k-blocks each: stream-K over 74 pairs
+    ((512, 8192, 32768), 2),     # 64 pair tiles on 74 pairs: one wave of v2 beats stream-K
+    ((1000, 3000, 32), 5),
 ])
 def test_auto_version_choice(vg, shape, want):
     assert vg.plan(-1, *shape, 256, 256, 256)["version"] == want
@@ -116,7 +120,7 @@ def test_plan_tails_and_alignment(vg):
 
 def test_plan_rejects_bad_input(vg):
     with pytest.raises(vg.VibeGemmError):
-        vg.plan(7, 16, 16, 16)
+        vg.plan(len(vg.versions()), 16, 16, 16)
     with pytest.raises(vg.VibeGemmError):
         vg.plan(0, -1, 16, 16)
 

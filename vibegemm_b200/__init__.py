@@ -27,6 +27,7 @@ _SIGS = {
     "vg_b200_gemm_f16_f32out": (ctypes.c_int, [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_b200_gemm_f16_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_cublas_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_cublas_gemm_f16_f32out": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_b200_num_versions": (ctypes.c_int, []),
     "vg_b200_version_name": (ctypes.c_char_p, [ctypes.c_int]),
     "vg_b200_default_version": (ctypes.c_int, []),
@@ -171,6 +172,16 @@ def cublas_gemm(A, B, out=None, stream=None):
     code = lib().vg_cublas_gemm_f16(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K,
                                     _stream_handle(stream))
     _check(code, "vg_cublas_gemm_f16")
+    return out
+
+
+def cublas_gemm_f32out(A, B, out=None, stream=None):
+    """cuBLAS with fp32 C (validation: its accumulation error beside gemm_f32out's)."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float32)
+    code = lib().vg_cublas_gemm_f16_f32out(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K,
+                                           _stream_handle(stream))
+    _check(code, "vg_cublas_gemm_f16_f32out")
     return out
 
 

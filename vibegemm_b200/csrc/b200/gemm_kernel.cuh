@@ -94,6 +94,7 @@ template <int CG, int BN_> struct TileCfg {
     static constexpr int BK = 64;           // fp16 per 128-B swizzle row
     static constexpr int NSUB = BN > 256 ? BN / 256 : 1; // MMAs per K step (N <= 256 each)
     static constexpr int ACC_BUFS = (NSUB == 1) ? 2 : 1;
+    static constexpr int NCHUNK = BN / 64; // 64-column epilogue chunks per tile
     static constexpr int B_ROWS = BN / CG;  // rows of B each CTA loads (one TMA box, <= 256)
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -122,8 +123,13 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
     static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
+    // Staging boxes per epilogue warp: two (a TMA store drains while the next box is
+    // written) unless that would not leave room for the pipeline stages.
+    static constexpr int kSmemLimit = 232448; // 227 KB of dynamic shared memory per CTA
+    static constexpr int EPI_BUFS =
+        (STAGES * (T::A_BYTES + T::B_BYTES) + T::EPI_WARPS * 2 * T::STG_BYTES + 2048 <= kSmemLimit) ? 2 : 1;
     static constexpr int EPI_BYTES = (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers || EPI == kEpiStagedF16)
-                                         ? T::EPI_WARPS * 2 * T::STG_BYTES
+                                         ? T::EPI_WARPS * EPI_BUFS * T::STG_BYTES
                                          : 0;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
     static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
@@ -131,6 +137,7 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
     static constexpr int ABORT_OFF = SLOT_OFF + 4;
     static constexpr int BYTES = ABORT_OFF + 4;
     static constexpr int DYN_BYTES = BYTES + 1024; // slack for 1024-B alignment
+    static_assert(DYN_BYTES <= kSmemLimit, "pipeline stages do not fit in shared memory");
 };
 
 __device__ unsigned int vg_status_word;
@@ -264,6 +271,13 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem_base = *slot_ptr;
+    // Programmatic dependent launch: the set-up above (barriers, TMEM, descriptor
+    // prefetch) may overlap the previous kernel of the stream; no global memory is read
+    // or written before that kernel has completed. Every CTA is resident when it lets the
+    // next grid be scheduled, so the next grid's CTAs never hold an SM that one of ours
+    // still waits for. Both are no-ops without the launch attribute.
+    ptx::grid_dep_wait();
+    ptx::grid_dep_launch();
 
     const int cluster_id = static_cast<int>(blockIdx.x) / CG;
     const int num_clusters = static_cast<int>(gridDim.x) / CG;
@@ -486,6 +500,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             ptx::tc_fence_after();
             const int row0 = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
             const int col0 = u.tile_n * T::BN;
+            const int cend = min(args.N, col0 + T::BN); // columns of this tile that exist
             // Owner of a split tile: the contributors' partials must have landed.
             if (SK && u.kind == kUnitOwner) {
                 for (int c = u.first_contrib; c <= u.last_contrib && epi_ok; ++c)
@@ -495,14 +510,14 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
 #pragma unroll 1
-            for (int c = 0; c < T::BN / 64; ++c) {
+            for (int c = 0; c < T::NCHUNK; ++c) {
                 uint32_t v0[32], v1[32];
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
                 ptx::tmem_wait_ld();
                 // Last read of a release unit (a whole buffer, or one half of the BN=512
                 // accumulator): hand those TMEM columns back to the MMA issuer.
-                if ((T::ACC_BUFS == 2) ? (c == T::BN / 64 - 1) : (c % 4 == 3)) {
+                if ((T::ACC_BUFS == 2) ? (c == T::NCHUNK - 1) : (c % 4 == 3)) {
                     const int unit = (T::ACC_BUFS == 2) ? acc : (c >> 2);
                     ptx::tc_fence_before();
                     __syncwarp();
@@ -560,7 +575,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
                         p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
                     }
-                    const uint32_t stg = sEpi + static_cast<uint32_t>(ew * 2 * T::STG_BYTES);
+                    const uint32_t stg = sEpi + static_cast<uint32_t>(ew * L::EPI_BUFS * T::STG_BYTES);
                     __syncwarp(); // previous chunk's reads of this buffer are done
                     const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
@@ -587,7 +602,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                                                static_cast<uint32_t>(col & 7) * 2u;
                             unsigned short bits;
                             asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(a));
-                            if (ccol + col < args.N)
+                            if (ccol + col < cend)
                                 reinterpret_cast<unsigned short *>(crow)[ccol + col] = bits;
                         }
                     }
@@ -598,9 +613,9 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
                         p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
                     }
-                    const uint32_t stg = sEpi + static_cast<uint32_t>((ew * 2 + buf) * T::STG_BYTES);
+                    const uint32_t stg = sEpi + static_cast<uint32_t>((ew * L::EPI_BUFS + buf) * T::STG_BYTES);
                     if (lane == 0)
-                        ptx::bulk_wait_group_read<1>();
+                        ptx::bulk_wait_group_read<L::EPI_BUFS - 1>();
                     __syncwarp();
                     const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
@@ -634,7 +649,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                                          : "r"(a));
                             const int grow = row0 + r;
                             const int gcol = ccol + 8 * j;
-                            if (grow < args.M && gcol < args.N) {
+                            if (grow < args.M && gcol < cend) {
                                 const long long off = static_cast<long long>(grow) * args.ldc + gcol;
                                 if (args.mc) {
                                     const __half *dst = static_cast<__half *>(args.mc) + off;
@@ -648,7 +663,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             }
                         }
                     }
-                    buf ^= 1;
+                    buf = (buf + 1) % L::EPI_BUFS;
                 } else if constexpr (EPI == kEpiDirectF16) {
                     const int row = row0 + lane;
                     if (row < args.M) {
@@ -657,7 +672,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         for (int j = 0; j < 8; ++j) {
                             const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
                             const int col = ccol + 8 * j;
-                            if (args.c_vec_ok && col + 8 <= args.N) {
+                            if (args.c_vec_ok && col + 8 <= cend) {
                                 uint4 q;
                                 q.x = pack_half2(v[0], v[1]);
                                 q.y = pack_half2(v[2], v[3]);
@@ -667,7 +682,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             } else {
 #pragma unroll
                                 for (int e = 0; e < 8; ++e)
-                                    if (col + e < args.N)
+                                    if (col + e < cend)
                                         crow[col + e] = __float2half_rn(__uint_as_float(v[e]));
                             }
                         }
@@ -680,7 +695,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         for (int j = 0; j < 8; ++j) {
                             const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
                             const int col = ccol + 8 * j;
-                            if (args.c_vec_ok && col + 8 <= args.N) {
+                            if (args.c_vec_ok && col + 8 <= cend) {
                                 float4 q0 = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]),
                                                         __uint_as_float(v[2]), __uint_as_float(v[3]));
                                 float4 q1 = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]),
@@ -690,7 +705,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             } else {
 #pragma unroll
                                 for (int e = 0; e < 8; ++e)
-                                    if (col + e < args.N)
+                                    if (col + e < cend)
                                         crow[col + e] = __uint_as_float(v[e]);
                             }
                         }

@@ -104,6 +104,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
     return ok != 0;
 }
 
+// ── programmatic dependent launch ─────────────────────────────────────────────
+// Wait until the grids this one depends on have completed and their memory is
+// visible (returns at once when the grid was launched without the attribute).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid of the stream, launched with the attribute, to be scheduled.
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ── TMA ───────────────────────────────────────────────────────────────────────
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

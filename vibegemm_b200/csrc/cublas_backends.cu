@@ -75,30 +75,70 @@ REGISTER_CUBLAS("cuBLAS", CublasBackend);
 
 // C ABI: one cuBLAS handle per (thread, device), stream set per call.
 // Returns 0, a cudaError_t code, or 1000 + cublasStatus_t for a cuBLAS failure.
+namespace {
+
+// One handle per (thread, device); 0 or the C-ABI error code in `code`.
+cublasHandle_t thread_handle(int &code) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        code = (int)e;
+        return nullptr;
+    }
+    constexpr int kMaxDev = 64;
+    thread_local cublasHandle_t handles[kMaxDev] = {};
+    if (dev < 0 || dev >= kMaxDev) {
+        code = (int)cudaErrorInvalidDevice;
+        return nullptr;
+    }
+    if (!handles[dev]) {
+        const cublasStatus_t s = cublasCreate(&handles[dev]);
+        if (s != CUBLAS_STATUS_SUCCESS) {
+            handles[dev] = nullptr;
+            code = 1000 + (int)s;
+            return nullptr;
+        }
+    }
+    code = 0;
+    return handles[dev];
+}
+
+} // namespace
+
 extern "C" int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
                                   vg_stream_t stream) {
     if (M < 0 || N < 0 || K < 0)
         return (int)cudaErrorInvalidValue;
     if (M == 0 || N == 0)
         return 0;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-        return (int)e;
-    constexpr int kMaxDev = 64;
-    thread_local cublasHandle_t handles[kMaxDev] = {};
-    if (dev < 0 || dev >= kMaxDev)
-        return (int)cudaErrorInvalidDevice;
-    if (!handles[dev]) {
-        const cublasStatus_t s = cublasCreate(&handles[dev]);
-        if (s != CUBLAS_STATUS_SUCCESS) {
-            handles[dev] = nullptr;
-            return 1000 + (int)s;
-        }
-    }
-    cublasStatus_t s = cublasSetStream(handles[dev], (cudaStream_t)stream);
+    int code = 0;
+    cublasHandle_t h = thread_handle(code);
+    if (!h)
+        return code;
+    cublasStatus_t s = cublasSetStream(h, (cudaStream_t)stream);
     if (s == CUBLAS_STATUS_SUCCESS)
-        s = gemm_ex(handles[dev], static_cast<const half *>(A), static_cast<const half *>(B),
+        s = gemm_ex(h, static_cast<const half *>(A), static_cast<const half *>(B),
                     static_cast<half *>(C), M, N, K);
+    return s == CUBLAS_STATUS_SUCCESS ? 0 : 1000 + (int)s;
+}
+
+// Validation twin of vg_cublas_gemm_f16: same operands and compute type, fp32 row-major C,
+// so cuBLAS's accumulation can be compared with the B200 kernels' fp32-output build.
+extern "C" int vg_cublas_gemm_f16_f32out(const void *A, const void *B, float *C, int M, int N,
+                                         int K, vg_stream_t stream) {
+    if (M < 0 || N < 0 || K < 0)
+        return (int)cudaErrorInvalidValue;
+    if (M == 0 || N == 0)
+        return 0;
+    int code = 0;
+    cublasHandle_t h = thread_handle(code);
+    if (!h)
+        return code;
+    const float alpha = 1.f, beta = 0.f;
+    cublasStatus_t s = cublasSetStream(h, (cudaStream_t)stream);
+    if (s == CUBLAS_STATUS_SUCCESS)
+        s = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, B, CUDA_R_16F, K, A,
+                         CUDA_R_16F, K, &beta, C, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
+                         CUBLAS_GEMM_DEFAULT);
     return s == CUBLAS_STATUS_SUCCESS ? 0 : 1000 + (int)s;
 }

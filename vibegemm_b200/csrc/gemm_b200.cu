@@ -66,6 +66,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v4", 2, 256, 6, true, true, 8, true},
     {"VibeGEMM B200 v5", 1, 192, 4, true, true, 8},
     {"VibeGEMM B200 v6", 2, 512, 4, false, true, 16},
+    {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -78,9 +79,10 @@ constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's 
 // Grids with fewer 256×256 tiles than pair slots cannot fill the GPU with one wave of
 // pairs; among the 256×256 pair (v2), 128×256 (v1) and 128×192 (v5) tiles pick the least
 // estimated time, waves × tile width / relative per-SM efficiency (pairs 1.1, 128×256 1.0,
-// 128×192 0.95: measured on the BASELINE shapes). Stream-K (v4) is never chosen: on B200
-// its fp32 fix-up traffic (128 KB per split tile and CTA) costs more than the idle SMs it
-// recovers on these sizes (measured with per-unit timestamps).
+// 128×192 0.95: measured on the BASELINE shapes), the same 128×192 tile with a fifth stage
+// (v7: one staging box per epilogue warp; +14 % at 1000×3000×8192, -3..5 % at K <= 2048,
+// where the shorter epilogue matters more) and stream-K (v4, only for long K over few
+// tiles: its fp32 fix-up costs about 28 k-blocks per split tile).
 int select_version(int M, int N, int K, int num_sms) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
@@ -98,12 +100,30 @@ int select_version(int M, int N, int K, int num_sms) {
     }
     if (t2 >= pairs)
         return 2;
+    // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
+    // (v1), pair 256×256 (v2), 128×192 (v5) and stream-K over pair tiles (v4), whose split
+    // tiles pay a fix-up of about 28 k-blocks (partials out, owner reads them back, the
+    // flag reset). Stream-K wins only when K is long and the tiles are few (e.g.
+    // 256×2048×32768); it also splits each output's accumulation chain, which makes it
+    // the more accurate choice there.
+    const long long kb = ceil_div_i(K, 64);
     const long long t1 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 256);
     const long long t5 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 192);
-    const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 / 1.1;
-    const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 / 1.0;
-    const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 / 0.95;
-    if (e5 < e1 && e5 < e2)
+    const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 * kb / 1.1;
+    const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 * kb / 1.0;
+    const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 * kb / 0.95;
+    // (stream-K only for grids at most half full: a single wave on most pairs runs at a
+    // higher clock under the power cap than the estimate credits, e.g. 512×8192×32768
+    // measured v2 1320 vs v4 1047 TFLOP/s)
+    const double e4 = (2 * t2 <= pairs) ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
+                                        : 1e300;
+    const double e7 = e5 * (kb >= 64 ? 0.88 : 1.04);
+    const double best = std::min({e1, e2, e4, e5, e7});
+    if (e7 == best)
+        return 7;
+    if (e4 == best)
+        return 4;
+    if (e5 == best)
         return 5;
     return e2 <= e1 ? 2 : 1;
 }
@@ -237,6 +257,17 @@ unsigned long long wait_timeout_ns() {
         g_timeout_ns.store(t, std::memory_order_relaxed);
     }
     return t;
+}
+
+// Programmatic dependent launch of the GEMM kernels (VG_PDL=0 turns it off): the kernel's
+// set-up overlaps the tail of the previous kernel in the stream, and the kernel waits for
+// that kernel's completion (griddepcontrol.wait) before it touches global memory.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *env = std::getenv("VG_PDL");
+        return !(env && env[0] == '0');
+    }();
+    return on;
 }
 
 // ── TMA descriptors ──────────────────────────────────────────────────────────
@@ -426,15 +457,22 @@ template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
         cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
         cfg.dynamicSmemBytes = kSmem;
         cfg.stream = s;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
+        unsigned n = 0;
         if (CG == 2) {
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 2;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
+            attr[n].id = cudaLaunchAttributeClusterDimension;
+            attr[n].val.clusterDim.x = 2;
+            attr[n].val.clusterDim.y = 1;
+            attr[n].val.clusterDim.z = 1;
+            ++n;
         }
+        if (pdl_enabled()) {
+            attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[n].val.programmaticStreamSerializationAllowed = 1;
+            ++n;
+        }
+        cfg.attrs = n ? attr : nullptr;
+        cfg.numAttrs = n;
         return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
     }
 };
@@ -489,6 +527,8 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
         return dispatch_epi<1, 192, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    if (p.cta_group == 1 && p.bn == 192 && p.stages == 5)
+        return dispatch_epi<1, 192, 5>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v3 and v6 (grid differs)
         return dispatch_epi<2, 512, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)

@@ -49,6 +49,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v6 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<6>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v6
+namespace gemm_b200_v7 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<7>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v7
 // The default entry point: one of the versions above, chosen per shape.
 namespace gemm_b200_auto {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
@@ -84,4 +87,5 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v3", GeneratedB200KernelBackend<gemm_b200_v3
 REGISTER_B200_KERNEL("VibeGEMM B200 v4", GeneratedB200KernelBackend<gemm_b200_v4::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v5", GeneratedB200KernelBackend<gemm_b200_v5::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v6", GeneratedB200KernelBackend<gemm_b200_v6::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v7", GeneratedB200KernelBackend<gemm_b200_v7::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
