@@ -103,8 +103,20 @@ template <int CG, int BN_> struct TileCfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int ACC_STRIDE = 256; // TMEM columns between the two accumulator buffers
     static constexpr uint32_t IDESC = idesc_f16_f32acc(BM * CG, BN / NSUB);
-    static constexpr int EPI_WARPS = 4;
+#ifndef VG_EPI_WARPS_PAIR
+#define VG_EPI_WARPS_PAIR 8
+#endif
+    // Epilogue warps: a multiple of 4, since warp w reads TMEM lanes [32·(w % 4), +32). With
+    // 4·G warps, group g = (w - 2) / 4 takes the 64-column chunks c ≡ g (mod G). CTA pairs
+    // use 8: their epilogue chunks take ~1.6-2.5x as long as a single CTA's (measured), and
+    // splitting a tile's chunks over two warp groups gained 3-8 % on short-K and unaligned
+    // shapes; single CTAs keep 4 (8 cost them 2-3 %).
+    static constexpr int EPI_WARPS = (CG == 2) ? VG_EPI_WARPS_PAIR : 4;
+    static constexpr int EPI_GROUPS = EPI_WARPS / 4;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    // Chunks per TMEM release unit: a whole buffer, or one 256-column half of the BN = 512
+    // accumulator.
+    static constexpr int CHUNKS_PER_UNIT = (ACC_BUFS == 2) ? NCHUNK : 4;
     static constexpr int STG_BYTES = 32 * 128; // one 32-row × 64-col fp16 box
 };
 
@@ -480,6 +492,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         // ───────────────────────── epilogue ─────────────────────────
         const int sub = warp & 3;    // TMEM sub-partition this warp may read
         const int ew = warp - 2;     // staging-buffer owner index
+        const int group = ew >> 2;   // which chunks of the tile this warp handles
         int acc = 0;
         uint32_t acc_phase = 0;
         int buf = 0;
@@ -510,15 +523,16 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
 #pragma unroll 1
-            for (int c = 0; c < T::NCHUNK; ++c) {
+            for (int c = group; c < T::NCHUNK; c += T::EPI_GROUPS) {
                 uint32_t v0[32], v1[32];
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
                 ptx::tmem_wait_ld();
-                // Last read of a release unit (a whole buffer, or one half of the BN=512
-                // accumulator): hand those TMEM columns back to the MMA issuer.
-                if ((T::ACC_BUFS == 2) ? (c == T::NCHUNK - 1) : (c % 4 == 3)) {
-                    const int unit = (T::ACC_BUFS == 2) ? acc : (c >> 2);
+                // This warp's last read of a release unit (a whole buffer, or one half of the
+                // BN=512 accumulator): hand those TMEM columns back to the MMA issuer.
+                const int unit_end = (c / T::CHUNKS_PER_UNIT + 1) * T::CHUNKS_PER_UNIT;
+                if (c + T::EPI_GROUPS >= unit_end) {
+                    const int unit = (T::ACC_BUFS == 2) ? acc : (c / T::CHUNKS_PER_UNIT);
                     ptx::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
