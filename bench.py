@@ -360,7 +360,8 @@ def run_b200(args) -> None:
         p0, prow = sh.__class__(M, N_DIM, K_DIM, peer, world).local
         gen.manual_seed(42 + peer)
         A_peer = torch.empty((prow, K_DIM), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=gen)
-        want = vg.gemm(A_peer, B)
+        v_fused = vg.plan(-1, prow, N_DIM, K_DIM, 256, 256, 256, allgather=True)["version"]
+        want = vg.gemm(A_peer, B, version=v_fused)  # same kernel version: bit-exact
         torch.cuda.synchronize()
         ok_rows = bool(torch.equal(fused.C[p0:p0 + prow], want))
         ok_all = max_over_ranks(0.0 if ok_rows else 1.0) == 0.0

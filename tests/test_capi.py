@@ -130,3 +130,16 @@ def test_gemm_rejects_cpu_tensors(vg):
     a = torch.zeros(4, 8, dtype=torch.float16)
     with pytest.raises(ValueError):
         vg.gemm(a, a)
+
+
+def test_allgather_plan_never_uses_stream_k(vg):
+    """The fused all-gather epilogue has no stream-K form: its per-shape choice skips v4
+    (a 501-row shard of 1001×1024×4099 would otherwise pick it) and an explicit v4 is refused."""
+    assert vg.plan(-1, 501, 1024, 4099, 256, 256, 256)["version"] == 4
+    p = vg.plan(-1, 501, 1024, 4099, 256, 256, 256, allgather=True)
+    assert p["version"] != 4 and p["stream_k"] == 0 and p["epilogue"] == "tma_f16_peers"
+    with pytest.raises(vg.VibeGemmError):
+        vg.plan(4, 501, 1024, 4099, 256, 256, 256, allgather=True)
+    import ctypes
+    out = (ctypes.c_int * 15)()
+    assert vg.lib().vg_b200_plan(-1, 512, 1024, 4096, 256, 256, 256, 3, 148, out) != 0  # no mode 3

@@ -3,7 +3,8 @@
 Each rank computes its row block of C with vg_b200_gemm_f16_allgather, whose epilogue also
 writes the rows into the other rank's full C over NVLink — one store per peer, or one
 NVLink-multicast (multimem) store when the node supports NVLS; after a barrier every rank's
-full C must equal a single-GPU GEMM of the whole problem, bit for bit.
+full C must equal a single-GPU GEMM of the whole problem with the same kernel version, bit
+for bit.
 """
 import os
 import socket
@@ -44,7 +45,12 @@ def _worker(rank, world, port, M, N, K, multicast, q):
         for _ in range(2):  # twice: repeated launches into the same buffers
             fused.run(dA, dB)
         fused.barrier()
-        full = vg.gemm(torch.from_numpy(A.view(np.int16).copy()).cuda().view(torch.float16), dB)
+        # Reference: the whole problem on this GPU with the version the shards resolved to.
+        # Every version except stream-K keeps one accumulation chain per output and agrees
+        # bit for bit, but the whole problem's own per-shape choice may be stream-K.
+        v = vg.plan(-1, rows, N, K, 256, 256, 256, allgather=True)["version"]
+        full = vg.gemm(torch.from_numpy(A.view(np.int16).copy()).cuda().view(torch.float16), dB,
+                       version=v)
         torch.cuda.synchronize()
         q.put((rank, bool(torch.equal(fused.C, full)), vg.device_status(), bool(fused.c_multicast_ptr)))
         fused.barrier()

@@ -342,9 +342,11 @@ def work_units(stream_k: bool, worker: int, workers: int, num_m: int, num_n: int
 
 
 def plan(version: int, M: int, N: int, K: int, a_ptr: int = 0, b_ptr: int = 0, c_ptr: int = 0,
-         f32_out: bool = False, num_sms: int = 148) -> dict:
+         f32_out: bool = False, num_sms: int = 148, allgather: bool = False) -> dict:
+    """Launch plan of vg_b200_plan (mode 1 = fp32 C, 2 = fused all-gather epilogue)."""
     out = (ctypes.c_int * len(PLAN_FIELDS))()
-    _check(lib().vg_b200_plan(version, M, N, K, a_ptr, b_ptr, c_ptr, int(f32_out), num_sms, out),
+    mode = 2 if allgather else int(bool(f32_out))
+    _check(lib().vg_b200_plan(version, M, N, K, a_ptr, b_ptr, c_ptr, mode, num_sms, out),
            "vg_b200_plan")
     d = dict(zip(PLAN_FIELDS, list(out)))
     d["epilogue"] = EPILOGUES[d["epilogue"]]

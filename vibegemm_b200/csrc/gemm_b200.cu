@@ -83,7 +83,7 @@ constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's 
 // (v7: one staging box per epilogue warp; +14 % at 1000×3000×8192, -3..5 % at K <= 2048,
 // where the shorter epilogue matters more) and stream-K (v4, only for long K over few
 // tiles: its fp32 fix-up costs about 28 k-blocks per split tile).
-int select_version(int M, int N, int K, int num_sms) {
+int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
@@ -115,8 +115,9 @@ int select_version(int M, int N, int K, int num_sms) {
     // (stream-K only for grids at most half full: a single wave on most pairs runs at a
     // higher clock under the power cap than the estimate credits, e.g. 512×8192×32768
     // measured v2 1320 vs v4 1047 TFLOP/s)
-    const double e4 = (2 * t2 <= pairs) ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
-                                        : 1e300;
+    const double e4 = (allow_stream_k && 2 * t2 <= pairs)
+                          ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
+                          : 1e300;
     const double e7 = e5 * (kb >= 64 ? 0.88 : 1.04);
     const double best = std::min({e1, e2, e4, e5, e7});
     if (e7 == best)
@@ -169,8 +170,8 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
               int num_sms, int max_clusters, Plan &p, bool peers = false) {
     if (M < 0 || N < 0 || K < 0 || num_sms <= 0)
         return cudaErrorInvalidValue;
-    if (version == kAutoVersion)
-        version = select_version(M, N, K, num_sms);
+    if (version == kAutoVersion) // the fused all-gather epilogue has no stream-K form
+        version = select_version(M, N, K, num_sms, !peers);
     if (version < 0 || version >= kNumVersions)
         return cudaErrorInvalidValue;
     const VersionDesc &v = kVersions[version];
@@ -992,9 +993,12 @@ void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *
 }
 
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
-                 int f32_out, int num_sms, int *out) {
+                 int mode, int num_sms, int *out) {
+    if (mode < 0 || mode > 2)
+        return (int)cudaErrorInvalidValue;
     vg::Plan p;
-    const int e = vg::make_plan(version, M, N, K, A, B, C, f32_out != 0, num_sms, num_sms / 2, p);
+    const int e = vg::make_plan(version, M, N, K, A, B, C, mode == 1, num_sms, num_sms / 2, p,
+                                mode == 2);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
     const int vals[15] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
