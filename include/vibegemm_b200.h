@@ -105,6 +105,15 @@ int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int 
 int vg_cublas_gemm_f16_f32out(const void *A, const void *B, float *C, int M, int N, int K,
                               vg_stream_t stream);
 
+/* cuBLASLt heuristic sweep, the "best cuBLAS" yardstick: up to `max_algos` algorithms that
+ * cublasLtMatmulAlgoGetHeuristic returns for this row-major problem (same operand order and
+ * compute type as vg_cublas_gemm_f16, 64 MiB workspace), each timed on `stream` after
+ * `warmup` launches over `iters` launches. ms_out[i] = mean ms per launch of algorithm i
+ * (-1 if it failed), *n_out = algorithms returned. Extends the reference's cuBLAS
+ * backend (csrc/cublas_backends.cu:21-35), which runs only cublasGemmEx's default choice. */
+int vg_cublaslt_sweep(const void *A, const void *B, void *C, int M, int N, int K, int max_algos,
+                      int warmup, int iters, float *ms_out, int *n_out, vg_stream_t stream);
+
 /* Registry listing: replaces KernelRegistry::make_all / GemmBackend::name
  * (include/registry.cuh:23-32, include/backend.cuh:16). vg_b200_default_version() is -1
  * (per-shape choice); vg_b200_version_name(-1) is "VibeGEMM B200 auto". */

@@ -77,3 +77,19 @@ def test_driver_binary_logs_text_and_json(vg, tmp_path):
     assert [r["backend"] for r in rows] == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
     assert all(r["passed"] and (r["M"], r["N"], r["K"]) == (512, 512, 512) for r in rows)
     assert rows[0]["pct_cublas"] == pytest.approx(100.0)
+
+
+@pytest.mark.gpu
+def test_cublaslt_sweep_times_algorithms_and_computes_the_gemm(vg):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.empty(1024, 768, dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    B = torch.empty(2048, 768, dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    C = torch.zeros(1024, 2048, dtype=torch.float16, device="cuda")
+    ms = vg.cublaslt_sweep(A, B, out=C, max_algos=8, warmup=1, iters=2)
+    torch.cuda.synchronize()
+    assert 1 <= len(ms) <= 8 and any(m > 0 for m in ms)
+    R = vg.cublas_gemm(A, B)
+    torch.cuda.synchronize()
+    d = (C.float() - R.float()).abs()
+    assert bool((d <= 1e-3 + 1e-2 * R.float().abs()).all())

@@ -28,6 +28,8 @@ _SIGS = {
     "vg_b200_gemm_f16_noalloc": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_cublas_gemm_f16": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
     "vg_cublas_gemm_f16_f32out": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]),
+    "vg_cublaslt_sweep": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 6
+                          + [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     "vg_b200_num_versions": (ctypes.c_int, []),
     "vg_b200_version_name": (ctypes.c_char_p, [ctypes.c_int]),
     "vg_b200_default_version": (ctypes.c_int, []),
@@ -183,6 +185,19 @@ def cublas_gemm_f32out(A, B, out=None, stream=None):
                                            _stream_handle(stream))
     _check(code, "vg_cublas_gemm_f16_f32out")
     return out
+
+
+def cublaslt_sweep(A, B, out=None, max_algos: int = 16, warmup: int = 3, iters: int = 10,
+                   stream=None) -> list[float]:
+    """Mean ms per launch of each cuBLASLt heuristic algorithm for C = A @ B.T (-1 = failed)."""
+    import torch
+    M, N, K, out = _operands(A, B, out, torch.float16)
+    ms = (ctypes.c_float * max_algos)()
+    n = ctypes.c_int(0)
+    code = lib().vg_cublaslt_sweep(A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K, max_algos,
+                                   warmup, iters, ms, ctypes.byref(n), _stream_handle(stream))
+    _check(code, "vg_cublaslt_sweep")
+    return [float(ms[i]) for i in range(n.value)]
 
 
 AUTO = -1  # per-shape version choice (the default entry point's policy)

@@ -75,11 +75,11 @@ def build(verbose: bool = False, driver: bool = True) -> Path:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs + ([CSRC / "main.cu"] if driver else [])))
     lib_objs = objs[: len(srcs)]
     if _stale(LIB, lib_objs):
-        _run([nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, lib_objs), "-lcublas"], verbose)
+        _run([nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, lib_objs), "-lcublas", "-lcublasLt"], verbose)
     if driver:
         BIN.parent.mkdir(exist_ok=True)
         if _stale(BIN, objs):
-            _run([nvcc(), *ARCH, "-o", str(BIN), *map(str, objs), "-lcublas"], verbose)
+            _run([nvcc(), *ARCH, "-o", str(BIN), *map(str, objs), "-lcublas", "-lcublasLt"], verbose)
     return LIB
 
 

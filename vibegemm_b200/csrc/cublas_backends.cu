@@ -142,3 +142,110 @@ extern "C" int vg_cublas_gemm_f16_f32out(const void *A, const void *B, float *C,
                          CUBLAS_GEMM_DEFAULT);
     return s == CUBLAS_STATUS_SUCCESS ? 0 : 1000 + (int)s;
 }
+
+// ── cuBLASLt heuristic sweep (a fairer "best cuBLAS" yardstick) ──────────────────────────
+// Asks cuBLASLt for up to `max_algos` algorithms for the row-major problem (the same
+// operand order as vg_cublas_gemm_f16: C^T = B^T·A in column-major terms, fp16 in/out,
+// CUBLAS_COMPUTE_32F, 64 MiB workspace) and times each one on `stream`: `warmup` untimed
+// launches, then `iters` launches between two events. ms_out[i] = mean ms of algorithm i
+// (or -1 if it failed); *n_out = number of algorithms returned. C holds the result of the
+// last algorithm timed.
+#include <cublasLt.h>
+
+extern "C" int vg_cublaslt_sweep(const void *A, const void *B, void *C, int M, int N, int K,
+                                 int max_algos, int warmup, int iters, float *ms_out, int *n_out,
+                                 vg_stream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || max_algos <= 0 || iters <= 0 || !ms_out || !n_out)
+        return (int)cudaErrorInvalidValue;
+    *n_out = 0;
+    constexpr size_t kWorkspace = 64ull << 20;
+    static thread_local void *workspace = nullptr;
+    static thread_local int workspace_dev = -1;
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess)
+        return (int)ce;
+    if (!workspace || workspace_dev != dev) {
+        ce = cudaMalloc(&workspace, kWorkspace);
+        if (ce != cudaSuccess) {
+            workspace = nullptr;
+            return (int)ce;
+        }
+        workspace_dev = dev;
+    }
+    cublasLtHandle_t lt = nullptr;
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+    cublasLtMatmulPreference_t pref = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    auto st = [&](cublasStatus_t s) {
+        if (s != CUBLAS_STATUS_SUCCESS && rc == 0)
+            rc = 1000 + (int)s;
+        return rc == 0;
+    };
+    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+    const size_t ws = kWorkspace;
+    if (st(cublasLtCreate(&lt)) && st(cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F)) &&
+        st(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta))) &&
+        st(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb))) &&
+        st(cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, K)) &&   // B: N×K row-major
+        st(cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, M, K)) &&   // A: M×K row-major
+        st(cublasLtMatrixLayoutCreate(&lc, CUDA_R_16F, N, M, N)) &&   // C: M×N row-major
+        st(cublasLtMatmulPreferenceCreate(&pref)) &&
+        st(cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws,
+                                                sizeof(ws)))) {
+        const int cap = max_algos < 64 ? max_algos : 64;
+        cublasLtMatmulHeuristicResult_t res[64];
+        int found = 0;
+        if (st(cublasLtMatmulAlgoGetHeuristic(lt, op, la, lb, lc, lc, pref, cap, res, &found))) {
+            ce = cudaEventCreate(&e0);
+            if (ce == cudaSuccess)
+                ce = cudaEventCreate(&e1);
+            if (ce != cudaSuccess)
+                rc = (int)ce;
+            const float alpha = 1.f, beta = 0.f;
+            cudaStream_t s = (cudaStream_t)stream;
+            for (int i = 0; i < found && rc == 0; ++i) {
+                auto run = [&]() {
+                    return cublasLtMatmul(lt, op, &alpha, B, la, A, lb, &beta, C, lc, C, lc, &res[i].algo,
+                                          workspace, kWorkspace, s);
+                };
+                bool ok = true;
+                for (int w = 0; w < warmup && ok; ++w)
+                    ok = run() == CUBLAS_STATUS_SUCCESS;
+                if (ok && cudaEventRecord(e0, s) == cudaSuccess) {
+                    for (int t = 0; t < iters && ok; ++t)
+                        ok = run() == CUBLAS_STATUS_SUCCESS;
+                    float ms = -1.f;
+                    if (ok && cudaEventRecord(e1, s) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess &&
+                        cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess)
+                        ms_out[i] = ms / iters;
+                    else
+                        ms_out[i] = -1.f;
+                } else {
+                    ms_out[i] = -1.f;
+                }
+                (void)cudaGetLastError();
+            }
+            *n_out = found;
+        }
+    }
+    if (e0)
+        cudaEventDestroy(e0);
+    if (e1)
+        cudaEventDestroy(e1);
+    if (pref)
+        cublasLtMatmulPreferenceDestroy(pref);
+    if (lc)
+        cublasLtMatrixLayoutDestroy(lc);
+    if (lb)
+        cublasLtMatrixLayoutDestroy(lb);
+    if (la)
+        cublasLtMatrixLayoutDestroy(la);
+    if (op)
+        cublasLtMatmulDescDestroy(op);
+    if (lt)
+        cublasLtDestroy(lt);
+    return rc;
+}

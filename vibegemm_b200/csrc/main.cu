@@ -5,8 +5,9 @@
 // this architecture, run each problem size. The B200 arm (sm >= 100) keeps
 // "B200" backends and cuBLAS, drops "A100"/"H100" names and logs to
 // results/perf_b200.txt. The default problem list is the reference's (8192³);
-// shapes can be given as arguments: `VibeGEMM [--normal] MxNxK ...`
-// (--normal = N(0, 0.02) inputs instead of uniform[-1,1]).
+// shapes can be given as arguments: `VibeGEMM [--normal] [--only SUBSTR] MxNxK ...`
+// (--normal = N(0, 0.02) inputs instead of uniform[-1,1]; --only keeps cuBLAS, the engine's
+// reference, and the backends whose names contain SUBSTR).
 // Besides the reference's text log, one JSON line per (backend, shape) goes to
 // results/perf_<arch>.jsonl: TFLOP/s, % of cuBLAS, % of the dense fp16 peak
 // (VG_PEAK_TFLOPS, else the nominal 2250 of B200), the check_error figures and the
@@ -119,9 +120,14 @@ int main(int argc, char **argv) {
 
     std::vector<GemmProblem> sizes;
     bool normal = false;
+    std::string only;
     for (int i = 1; i < argc; ++i) {
         if (std::strcmp(argv[i], "--normal") == 0) {
             normal = true;
+            continue;
+        }
+        if (std::strcmp(argv[i], "--only") == 0 && i + 1 < argc) {
+            only = argv[++i];
             continue;
         }
         int m = 0, n = 0, k = 0;
@@ -167,6 +173,8 @@ int main(int argc, char **argv) {
         if (sm >= 90 && sm < 100 && (is_a100 || is_b200))
             continue;
         if (sm < 90 && (is_h100 || is_b200))
+            continue;
+        if (!only.empty() && name != "cuBLAS" && name.find(only) == std::string::npos)
             continue;
         engine.add_backend(b);
     }
