@@ -381,24 +381,27 @@ cudaError_t workspace_pool(int dev, cudaMemPool_t &pool) {
 // may be arbitrarily aligned).
 __global__ void pad_rows_f16(const __half *__restrict__ src, long long rows, int cols,
                              long long ld_src, __half *__restrict__ dst, int ld_dst) {
-    const long long groups_per_row = ld_dst / 8;
-    const long long total = rows * groups_per_row;
+    // Blocks stride over rows, threads over 8-element groups of a row (no index division).
+    // Source rows may start on any 2-B boundary, so the loads are 2-B; the warp's loads of a
+    // row cover 512 contiguous bytes per element step and coalesce in L1. Stores are 16 B.
+    const int groups_per_row = ld_dst / 8;
     const unsigned short *s16 = reinterpret_cast<const unsigned short *>(src);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / groups_per_row;
-        const int c0 = (int)(i - r * groups_per_row) * 8;
+    for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         const unsigned short *row = s16 + r * ld_src;
-        unsigned short v[8];
+        uint4 *out = reinterpret_cast<uint4 *>(dst + r * ld_dst);
+        for (int g = threadIdx.x; g < groups_per_row; g += blockDim.x) {
+            const int c0 = g * 8;
+            unsigned short v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-            v[e] = (c0 + e < cols) ? row[c0 + e] : (unsigned short)0;
-        uint4 q;
-        q.x = v[0] | ((unsigned)v[1] << 16);
-        q.y = v[2] | ((unsigned)v[3] << 16);
-        q.z = v[4] | ((unsigned)v[5] << 16);
-        q.w = v[6] | ((unsigned)v[7] << 16);
-        *reinterpret_cast<uint4 *>(dst + r * ld_dst + c0) = q;
+            for (int e = 0; e < 8; ++e)
+                v[e] = (c0 + e < cols) ? row[c0 + e] : (unsigned short)0;
+            uint4 q;
+            q.x = v[0] | ((unsigned)v[1] << 16);
+            q.y = v[2] | ((unsigned)v[3] << 16);
+            q.z = v[4] | ((unsigned)v[5] << 16);
+            q.w = v[6] | ((unsigned)v[7] << 16);
+            out[g] = q;
+        }
     }
 }
 
@@ -406,10 +409,8 @@ cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, i
                        int num_sms, cudaStream_t s) {
     if (rows == 0)
         return cudaSuccess;
-    const long long total = rows * (ld_dst / 8);
     const int threads = 256;
-    const long long want = (total + threads - 1) / threads;
-    const int blocks = (int)std::min<long long>(want, (long long)num_sms * 8);
+    const int blocks = (int)std::min<long long>(rows, (long long)num_sms * 16);
     pad_rows_f16<<<blocks, threads, 0, s>>>(static_cast<const __half *>(src), rows, cols, cols, dst,
                                             ld_dst);
     return cudaGetLastError();
@@ -559,9 +560,45 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
     return w;
 }
 
-cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
-                     bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0,
-                     void *c_multicast = nullptr) {
+// ── workspaces ───────────────────────────────────────────────────────────────
+// Pad workspace of vg_b200_gemm_f16_noalloc: a fixed array in the module's device
+// memory instead of the stream-ordered pool. Every GPU that loads this library holds
+// these kNoAllocScratchBytes until the process exits. In host code the name
+// `noalloc_scratch` is only a host-side stand-in for the symbol; its device address
+// comes from cudaGetSymbolAddress, taken once per device with that device current.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
+static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
+
+struct ScratchAddr {
+    void *ptr = nullptr;
+    cudaError_t err = cudaSuccess;
+};
+ScratchAddr g_scratch[kMaxDevices];
+std::once_flag g_scratch_once[kMaxDevices];
+
+const ScratchAddr &noalloc_scratch_addr(int dev) {
+    std::call_once(g_scratch_once[dev], [dev] {
+        ScratchAddr &s = g_scratch[dev];
+        s.err = cudaGetSymbolAddress(&s.ptr, noalloc_scratch);
+        if (s.err != cudaSuccess) {
+            s.ptr = nullptr;
+            (void)cudaGetLastError();
+        }
+    });
+    return g_scratch[dev];
+}
+
+// Where a call's workspace (K-padded operands, stream-K partials and flags) lives: the
+// library's stream-ordered pool (allocated and freed on the caller's stream) or the fixed
+// no-allocation array (nothing is allocated; problems that need more return
+// VG_ERROR_NOALLOC_SCRATCH_LIMIT).
+enum class WsSource { Pool, Scratch };
+
+// One GEMM launch: validation, plan, workspace, pre-passes, tensor maps, kernel.
+// Returns a cudaError_t value or VG_ERROR_NOALLOC_SCRATCH_LIMIT.
+int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
+                bool f32_out, cudaStream_t s, void *const *peers, int num_peers, void *c_multicast,
+                WsSource src) {
     if ((version != kAutoVersion && (version < 0 || version >= kNumVersions)) || M < 0 || N < 0 || K < 0)
         return cudaErrorInvalidValue;
     if (M == 0 || N == 0)
@@ -606,22 +643,32 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     if (p.cta_group == 2 && p.persistent && max_clusters > 0)
         grid = std::min(grid, 2 * max_clusters);
 
-    // One stream-ordered workspace: K-padded copies of operands TMA cannot describe, and
-    // the stream-K partial slots + ready flags (zeroed here, every launch).
+    // One workspace: K-padded copies of operands TMA cannot describe, and the stream-K
+    // partial slots + ready flags (zeroed here, every launch).
     const void *A_use = A, *B_use = B;
-    void *ws = nullptr;
     const int Kp = p.Kp;
     const WsLayout wl = workspace_layout(p, M, N, grid);
+    if (src == WsSource::Scratch && wl.total > kNoAllocScratchBytes)
+        return VG_ERROR_NOALLOC_SCRATCH_LIMIT;
+    void *owned = nullptr; // pool allocation to free after the launch
     float *sk_partials = nullptr;
     unsigned *sk_flags = nullptr;
     if (wl.total) {
-        cudaMemPool_t pool;
-        e = workspace_pool(dev, pool);
-        if (e == cudaSuccess)
-            e = cudaMallocFromPoolAsync(&ws, wl.total, pool, s);
-        if (e != cudaSuccess)
-            return e;
-        char *base = static_cast<char *>(ws);
+        char *base = nullptr;
+        if (src == WsSource::Pool) {
+            cudaMemPool_t pool;
+            e = workspace_pool(dev, pool);
+            if (e == cudaSuccess)
+                e = cudaMallocFromPoolAsync(&owned, wl.total, pool, s);
+            if (e != cudaSuccess)
+                return e;
+            base = static_cast<char *>(owned);
+        } else {
+            const ScratchAddr &sc = noalloc_scratch_addr(dev);
+            if (sc.err != cudaSuccess)
+                return sc.err;
+            base = static_cast<char *>(sc.ptr);
+        }
         __half *wa = reinterpret_cast<__half *>(base + wl.a_off);
         __half *wb = reinterpret_cast<__half *>(base + wl.b_off);
         if (p.pad_a) {
@@ -639,7 +686,8 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
                 e = cudaMemsetAsync(sk_flags, 0, wl.flag_bytes, s);
         }
         if (e != cudaSuccess) {
-            (void)cudaFreeAsync(ws, s);
+            if (owned)
+                (void)cudaFreeAsync(owned, s);
             return e;
         }
     }
@@ -652,8 +700,8 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     if (ok && (p.epi == kEpiTmaF16 || p.epi == kEpiTmaF16Peers))
         ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
     if (!ok) {
-        if (ws)
-            (void)cudaFreeAsync(ws, s);
+        if (owned)
+            (void)cudaFreeAsync(owned, s);
         return cudaErrorInvalidValue;
     }
 
@@ -677,140 +725,25 @@ cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, 
     args.mc = c_multicast;
 
     e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
-    if (ws) {
-        const cudaError_t f = cudaFreeAsync(ws, s);
+    if (owned) {
+        const cudaError_t f = cudaFreeAsync(owned, s);
         if (e == cudaSuccess)
             e = f;
     }
     return e;
 }
 
-// ── allocation-free variant ─────────────────────────────────────────────────
-// Pad workspace of vg_b200_gemm_f16_noalloc: a fixed array in the module's device
-// memory instead of the stream-ordered pool. Every GPU that loads this library holds
-// these kNoAllocScratchBytes until the process exits. In host code the name
-// `noalloc_scratch` is only a host-side stand-in for the symbol; its device address
-// comes from cudaGetSymbolAddress, taken once per device with that device current.
-constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
-static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
-
-struct ScratchAddr {
-    void *ptr = nullptr;
-    cudaError_t err = cudaSuccess;
-};
-ScratchAddr g_scratch[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
-
-const ScratchAddr &noalloc_scratch_addr(int dev) {
-    std::call_once(g_scratch_once[dev], [dev] {
-        ScratchAddr &s = g_scratch[dev];
-        s.err = cudaGetSymbolAddress(&s.ptr, noalloc_scratch);
-        if (s.err != cudaSuccess) {
-            s.ptr = nullptr;
-            (void)cudaGetLastError();
-        }
-    });
-    return g_scratch[dev];
+cudaError_t run_gemm(int version, const void *A, const void *B, void *C, int M, int N, int K,
+                     bool f32_out, cudaStream_t s, void *const *peers = nullptr, int num_peers = 0,
+                     void *c_multicast = nullptr) {
+    return (cudaError_t)launch_gemm(version, A, B, C, M, N, K, f32_out, s, peers, num_peers,
+                                    c_multicast, WsSource::Pool);
 }
 
-// Same plan, descriptors and launches as run_gemm for the default version, with the
-// K-padding workspace taken from noalloc_scratch; nothing is allocated or freed.
-// Returns a cudaError_t value or VG_ERROR_NOALLOC_SCRATCH_LIMIT.
+// The default entry point's launch with the workspace in the fixed array.
 int run_gemm_noalloc(const void *A, const void *B, void *C, int M, int N, int K, cudaStream_t s) {
-    const int version = kAutoVersion;
-    if (M < 0 || N < 0 || K < 0)
-        return cudaErrorInvalidValue;
-    if (M == 0 || N == 0)
-        return cudaSuccess;
-    if (!C)
-        return cudaErrorInvalidValue;
-    if (K == 0)
-        return cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), s);
-    if (!A || !B)
-        return cudaErrorInvalidValue;
-
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-        return e;
-    const DeviceInfo *di = device_info(dev);
-    if (!di || !di->ok)
-        return cudaErrorInvalidDevice;
-    if (di->major != 10 || di->minor != 0)
-        return cudaErrorNoKernelImageForDevice;
-
-    Plan p;
-    e = (cudaError_t)make_plan(version, M, N, K, (uintptr_t)A, (uintptr_t)B, (uintptr_t)C, false,
-                               di->num_sms, di->num_sms / 2, p);
-    if (e != cudaSuccess)
-        return e;
-    const int Kp = p.Kp;
-    int max_clusters = 0;
-    e = dispatch(p, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
-    if (e != cudaSuccess)
-        return e;
-    int grid = p.grid;
-    if (p.cta_group == 2 && p.persistent && max_clusters > 0)
-        grid = std::min(grid, 2 * max_clusters);
-    // Same workspace as run_gemm (padded operands, stream-K partials and flags), placed in
-    // the fixed array; it must fit.
-    const WsLayout wl = workspace_layout(p, M, N, grid);
-    if (wl.total > kNoAllocScratchBytes)
-        return VG_ERROR_NOALLOC_SCRATCH_LIMIT;
-
-    const void *A_use = A, *B_use = B;
-    float *sk_partials = nullptr;
-    unsigned *sk_flags = nullptr;
-    if (wl.total) {
-        const ScratchAddr &sc = noalloc_scratch_addr(dev);
-        if (sc.err != cudaSuccess)
-            return sc.err;
-        char *base = static_cast<char *>(sc.ptr);
-        __half *wa = reinterpret_cast<__half *>(base + wl.a_off);
-        __half *wb = reinterpret_cast<__half *>(base + wl.b_off);
-        if (p.pad_a) {
-            e = launch_pad(A, M, K, wa, Kp, di->num_sms, s);
-            A_use = wa;
-        }
-        if (e == cudaSuccess && p.pad_b) {
-            e = launch_pad(B, N, K, wb, Kp, di->num_sms, s);
-            B_use = wb;
-        }
-        if (p.stream_k) {
-            sk_partials = reinterpret_cast<float *>(base + wl.part_off);
-            sk_flags = reinterpret_cast<unsigned *>(base + wl.flag_off);
-            if (e == cudaSuccess) // flags start at zero every call (not an allocation)
-                e = cudaMemsetAsync(sk_flags, 0, wl.flag_bytes, s);
-        }
-        if (e != cudaSuccess)
-            return e;
-    }
-
-    CUtensorMap ma, mb, mc;
-    std::memset(&mc, 0, sizeof(mc));
-    const uint32_t b_box_rows = (uint32_t)(p.bn / p.cta_group);
-    bool ok = get_map(ma, A_use, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp, 64u, 128u, dev) &&
-              get_map(mb, B_use, (uint64_t)Kp, (uint64_t)N, (uint64_t)Kp, 64u, b_box_rows, dev);
-    if (ok && p.epi == kEpiTmaF16)
-        ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
-    if (!ok)
-        return cudaErrorInvalidValue;
-
-    GemmArgs args{};
-    args.M = M;
-    args.N = N;
-    args.K = Kp;
-    args.num_m_tiles = p.num_m_tiles;
-    args.num_n_tiles = p.num_n_tiles;
-    args.num_kb = p.num_kb;
-    args.group_m = p.group_m;
-    args.c_vec_ok = (N % 8 == 0) && aligned16((uintptr_t)C);
-    args.C = C;
-    args.ldc = N;
-    args.timeout_ns = wait_timeout_ns();
-    args.sk_partials = sk_partials;
-    args.sk_flags = sk_flags;
-    return dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+    return launch_gemm(kAutoVersion, A, B, C, M, N, K, false, s, nullptr, 0, nullptr,
+                       WsSource::Scratch);
 }
 
 } // namespace
