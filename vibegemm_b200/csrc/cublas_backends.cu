@@ -166,6 +166,9 @@ extern "C" int vg_cublaslt_sweep(const void *A, const void *B, void *C, int M, i
     if (ce != cudaSuccess)
         return (int)ce;
     if (!workspace || workspace_dev != dev) {
+        if (workspace)
+            (void)cudaFree(workspace); // the previous device's workspace (unified addressing)
+        workspace = nullptr;
         ce = cudaMalloc(&workspace, kWorkspace);
         if (ce != cudaSuccess) {
             workspace = nullptr;
