@@ -184,11 +184,12 @@ int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, i
  * with `num_sms` SMs (exposed so the planner can be tested without a GPU).
  * `version` may be -1 (per-shape choice). `mode`: 0 = fp16 C (vg_b200_gemm_f16),
  * 1 = fp32 C (vg_b200_gemm_f16_f32out), 2 = fp16 C with the fused all-gather
- * (vg_b200_gemm_f16_allgather, whose per-shape choice excludes stream-K). Fields of `out` (int[15]): cta_group, stages,
- * epilogue kind (0 TMA fp16, 1 direct fp16, 2 direct fp32, 3 TMA fp16 + peer stores,
- * 4 staged fp16 with coalesced row stores for C rows TMA cannot describe),
- * pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb, group_m, grid (CTAs),
- * persistent, tile columns, resolved version, stream-K. Returns 0 or a cudaError_t code. */
+ * (vg_b200_gemm_f16_allgather, whose per-shape choice excludes stream-K).
+ * Fields of `out` (int[16]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct fp16,
+ * 2 direct fp32, 3 TMA fp16 + peer stores, 4 staged fp16 with coalesced row stores for C
+ * rows TMA cannot describe), pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb,
+ * group_m, grid (CTAs), persistent, tile columns, resolved version, stream-K, promote
+ * (chunked accumulation with an fp32 running sum). Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int mode, int num_sms, int *out);
 

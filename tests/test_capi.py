@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol(vg):
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
-                             "VibeGEMM B200 v6", "VibeGEMM B200 v7"]
+                             "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -141,5 +141,5 @@ def test_allgather_plan_never_uses_stream_k(vg):
     with pytest.raises(vg.VibeGemmError):
         vg.plan(4, 501, 1024, 4099, 256, 256, 256, allgather=True)
     import ctypes
-    out = (ctypes.c_int * 15)()
+    out = (ctypes.c_int * 16)()
     assert vg.lib().vg_b200_plan(-1, 512, 1024, 4096, 256, 256, 256, 3, 148, out) != 0  # no mode 3

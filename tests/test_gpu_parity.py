@@ -17,7 +17,7 @@ from conftest import to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
-VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, -1]  # -1: the default entry point's per-shape choice
+VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, -1]  # -1: the default entry point's per-shape choice
 # (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
 # epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
 SHAPES = [
@@ -169,7 +169,8 @@ def test_long_k_acceptance(vg, orc, shape):
     error |c - r| / max(|r|, abs bound) is within 1e-2, or no worse than cuBLAS's fp16 GEMM
     on the same rows. (One accumulation chain per output over K = 32768 reaches 1.3e-2 on
     a few elements, because the tensor cores' accumulation rounds toward zero; cuBLAS keeps
-    one chain at 512×8192 and splits K at 256×2048, as stream-K does here.)"""
+    one chain at 512×8192 and splits K at 256×2048, as stream-K does here.) v8, which adds
+    4096-long chunks into an fp32 running sum, meets max rel <= 1e-2 outright."""
     import torch
     M, N, K = shape
     A, B = orc.make_inputs(M, N, K)
@@ -184,6 +185,8 @@ def test_long_k_acceptance(vg, orc, shape):
         acc = orc.acceptance(c, exact, K=K)
         assert acc["max_abs"] <= bound, (v, acc)
         assert np.all(np.abs(c - exact) <= bound + 1e-2 * np.abs(exact)), (v, acc)
+        if v == 8:  # chunked accumulation with an fp32 running sum: the strict bound holds
+            assert acc["max_rel"] <= 1e-2, (v, acc)
     cb16 = vg.cublas_gemm(dA, dB)
     C16 = vg.gemm(dA, dB)
     torch.cuda.synchronize()

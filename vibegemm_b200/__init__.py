@@ -64,7 +64,8 @@ _SIGS = {
 EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
-               "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version", "stream_k")
+               "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version", "stream_k",
+               "promote")
 EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32", 3: "tma_f16_peers", 4: "staged_f16"}
 
 

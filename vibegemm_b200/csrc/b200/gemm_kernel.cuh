@@ -84,6 +84,7 @@ struct GemmArgs {
     // major) and ready flags (zeroed before the launch).
     float *sk_partials;
     unsigned *sk_flags;
+    int promote_kb; // PROMOTE kernels: k-blocks per accumulation chunk
 };
 
 template <int CG, int BN_> struct TileCfg {
@@ -221,7 +222,13 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
     }
 }
 
-template <int CG, int BN, int STAGES, int EPI, bool SK = false>
+// PROMOTE: each tile's K range is cut into chunks of args.promote_kb k-blocks; every chunk
+// is accumulated by the tensor cores from zero in TMEM buffer 0, and the epilogue warps add
+// it in fp32 (round to nearest) into a running sum kept in TMEM buffer 1. Each output then
+// sums short tensor-core chains instead of one long one (the tensor cores' accumulation
+// rounds toward zero, an error that grows with the chain). No accumulator double buffering:
+// the MMA waits while a chunk is added in. Requires ACC_BUFS == 2 and no stream-K.
+template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false>
 __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
@@ -229,6 +236,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
     using T = TileCfg<CG, BN>;
     using L = SmemLayout<CG, BN, STAGES, EPI>;
+    static_assert(!PROMOTE || (T::ACC_BUFS == 2 && !SK), "PROMOTE needs two TMEM buffers, no stream-K");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = ptx::smem_u32(smem_raw);
@@ -394,7 +402,34 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             WorkUnit u;
             while (ok && it.next(u)) {
                 const int nkb = u.kb1 - u.kb0; // k-blocks of this unit; MMAs index them from 0
-                if constexpr (T::ACC_BUFS == 2) {
+                if constexpr (PROMOTE) {
+                    for (int c0 = 0; c0 < nkb && ok; c0 += args.promote_kb) {
+                        const int c1 = min(nkb, c0 + args.promote_kb);
+                        if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo,
+                                      kStatusTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        for (int kb = c0; kb < c1; ++kb) {
+                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                            issue(tmem_base, 0, kb - c0); // a fresh chain at each chunk start
+                            any = true;
+                            commit_to(empty_bar(stage));
+                            advance();
+                        }
+                        if (!ok)
+                            break;
+                        commit_to(tfull_bar(0));
+                        acc_phase ^= 1u;
+                    }
+                    if (!ok)
+                        break;
+                } else if constexpr (T::ACC_BUFS == 2) {
                     if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
                                   kStatusTimeoutMma)) {
                         ok = false;
@@ -507,9 +542,14 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         };
         bool epi_ok = true;
         while (epi_ok && it.next(u)) {
+          // PROMOTE: one pass per K chunk; only the last one stores C.
+          const int nkc = PROMOTE ? (u.kb1 - u.kb0 + args.promote_kb - 1) / args.promote_kb : 1;
+          for (int j = 0; j < nkc && epi_ok; ++j) {
             if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
-                          VG_EPI_BACKOFF_NS))
+                          VG_EPI_BACKOFF_NS)) {
+                epi_ok = false;
                 break;
+            }
             ptx::tc_fence_after();
             const int row0 = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
             const int col0 = u.tile_n * T::BN;
@@ -540,6 +580,28 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             ptx::mbar_arrive(tempty_bar(unit));
                         else
                             ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
+                    }
+                }
+                if constexpr (PROMOTE) {
+                    // Running sum of the earlier chunks: buffer 1, same lanes and columns.
+                    const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                                           static_cast<uint32_t>(T::ACC_STRIDE + c * 64);
+                    if (j > 0) {
+                        uint32_t s0[32], s1[32];
+                        ptx::tmem_ld_32x32b_x32(s_row, s0);
+                        ptx::tmem_ld_32x32b_x32(s_row + 32, s1);
+                        ptx::tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            v0[i] = __float_as_uint(__uint_as_float(v0[i]) + __uint_as_float(s0[i]));
+                            v1[i] = __float_as_uint(__uint_as_float(v1[i]) + __uint_as_float(s1[i]));
+                        }
+                    }
+                    if (j + 1 < nkc) {
+                        ptx::tmem_st_32x32b_x32(s_row, v0);
+                        ptx::tmem_st_32x32b_x32(s_row + 32, v1);
+                        ptx::tmem_wait_st();
+                        continue; // not the last chunk: nothing to store yet
                     }
                 }
                 const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
@@ -736,13 +798,16 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                                  : "memory");
                 }
             }
-            if constexpr (T::ACC_BUFS == 2) {
+            if constexpr (PROMOTE) {
+                acc_phase ^= 1u; // every chunk lands in buffer 0
+            } else if constexpr (T::ACC_BUFS == 2) {
                 acc ^= 1;
                 if (acc == 0)
                     acc_phase ^= 1u;
             } else {
                 acc_phase ^= 1u;
             }
+          } // K chunks
         }
         if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
             if (lane == 0)

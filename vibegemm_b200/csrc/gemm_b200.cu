@@ -56,6 +56,7 @@ struct VersionDesc {
     bool tma_store;
     int group_m;
     bool stream_k = false;
+    bool promote = false; // chunked accumulation with an fp32 running sum (accurate long K)
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -67,6 +68,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v5", 1, 192, 4, true, true, 8},
     {"VibeGEMM B200 v6", 2, 512, 4, false, true, 16},
     {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
+    {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -130,6 +132,9 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
 }
 
 constexpr int kMinSkIters = 4; // k-blocks per stream-K worker at least
+// Promoting versions: k-blocks (of 64) per tensor-core accumulation chunk. K = 4096 per
+// chunk cuts the rounding-toward-zero drift of one 32768-long chain to about a third.
+constexpr int kPromoteKb = 64;
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
 
@@ -161,6 +166,7 @@ struct Plan {
     int group_m = 8;
     int grid = 0;
     int persistent = 0;
+    int promote = 0;
 };
 
 inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
@@ -203,6 +209,7 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.num_kb = ceil_div_i(p.Kp, 64);
     const long long tiles = (long long)p.num_m_tiles * p.num_n_tiles;
     p.stream_k = v.stream_k ? 1 : 0;
+    p.promote = v.promote ? 1 : 0;
     if (v.stream_k) {
         if (peers)
             return cudaErrorInvalidValue;
@@ -417,7 +424,7 @@ cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, i
 }
 
 // ── kernel launch ────────────────────────────────────────────────────────────
-template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE> struct Inst {
     static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
     static std::atomic<unsigned long long> attr_ready; // bit per device
     static int max_clusters[kMaxDevices];
@@ -425,7 +432,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
     static cudaError_t prepare(int dev) {
         if ((attr_ready.load(std::memory_order_acquire) >> dev) & 1ull)
             return cudaSuccess;
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
@@ -453,7 +460,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
 
     static cudaError_t launch(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                               const GemmArgs &args, int grid, cudaStream_t s) {
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE>;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid, 1, 1);
         cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
@@ -478,24 +485,24 @@ template <int CG, int BN, int STAGES, int EPI, bool SK> struct Inst {
         return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
     }
 };
-template <int CG, int BN, int STAGES, int EPI, bool SK>
-std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK>::attr_ready{0};
-template <int CG, int BN, int STAGES, int EPI, bool SK>
-int Inst<CG, BN, STAGES, EPI, SK>::max_clusters[kMaxDevices] = {};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE>
+std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK, PROMOTE>::attr_ready{0};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE>
+int Inst<CG, BN, STAGES, EPI, SK, PROMOTE>::max_clusters[kMaxDevices] = {};
 
-template <int CG, int BN, int STAGES, bool SK = false>
+template <int CG, int BN, int STAGES, bool SK = false, bool PROMOTE = false>
 cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
                          const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                          const GemmArgs *args, int grid, cudaStream_t s) {
 #define VG_EPI_CASE(E)                                                                             \
     case E: {                                                                                      \
-        cudaError_t e = Inst<CG, BN, STAGES, E, SK>::prepare(dev);                                 \
+        cudaError_t e = Inst<CG, BN, STAGES, E, SK, PROMOTE>::prepare(dev);                        \
         if (e != cudaSuccess)                                                                      \
             return e;                                                                              \
-        max_clusters = Inst<CG, BN, STAGES, E, SK>::max_clusters[dev];                             \
+        max_clusters = Inst<CG, BN, STAGES, E, SK, PROMOTE>::max_clusters[dev];                    \
         if (query_only)                                                                            \
             return cudaSuccess;                                                                    \
-        return Inst<CG, BN, STAGES, E, SK>::launch(*ma, *mb, *mc, *args, grid, s);                 \
+        return Inst<CG, BN, STAGES, E, SK, PROMOTE>::launch(*ma, *mb, *mc, *args, grid, s);        \
     }
     if constexpr (SK) {
         switch (epi) {
@@ -527,6 +534,9 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 4)
         return dispatch_epi<1, 192, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
+    if (p.promote && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
+        return dispatch_epi<2, 256, 6, false, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args,
+                                                    grid, s);
     if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 5)
@@ -719,6 +729,7 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     args.timeout_ns = wait_timeout_ns();
     args.sk_partials = sk_partials;
     args.sk_flags = sk_flags;
+    args.promote_kb = kPromoteKb;
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
@@ -934,9 +945,10 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
                                 mode == 2);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[15] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
+    const int vals[16] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
                           p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
-                          p.grid,      p.persistent,  p.bn,          p.version, p.stream_k};
+                          p.grid,      p.persistent,  p.bn,          p.version, p.stream_k,
+                          p.promote};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }

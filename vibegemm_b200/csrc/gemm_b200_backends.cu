@@ -52,6 +52,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v7 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<7>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v7
+namespace gemm_b200_v8 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<8>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v8
 // The default entry point: one of the versions above, chosen per shape.
 namespace gemm_b200_auto {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
@@ -88,4 +91,5 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v4", GeneratedB200KernelBackend<gemm_b200_v4
 REGISTER_B200_KERNEL("VibeGEMM B200 v5", GeneratedB200KernelBackend<gemm_b200_v5::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v6", GeneratedB200KernelBackend<gemm_b200_v6::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v7", GeneratedB200KernelBackend<gemm_b200_v7::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v8", GeneratedB200KernelBackend<gemm_b200_v8::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
