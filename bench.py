@@ -55,6 +55,12 @@ FALLBACK_PEAK_TFLOPS = 1590.0  # used only when MEASURED_PEAKS.json is absent
 PROFILE_SUMMARY = ROOT / "profiles" / "gemm_b200_v3_8192.md"
 
 
+def workload_name(workload: str) -> str:
+    """The `config.workload` string, shared by both arms of the bench."""
+    return {"gemm8192": "fp16_gemm_8192x8192x8192_per_gpu",
+            "sharded32k": "fp16_gemm_32768x32768x32768_row_sharded"}[workload]
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -188,7 +194,9 @@ def run_reference(args) -> None:
     import oracle
 
     threads = oracle.max_threads()
-    A, B = oracle.make_inputs(64, N_DIM, K_DIM)
+    rows_per_gpu, m_total, n_dim, k_dim, scaling = WORKLOADS[args.workload]
+    m_full = m_total if m_total is not None else rows_per_gpu
+    A, B = oracle.make_inputs(64, n_dim, k_dim)
     t0 = time.perf_counter()
     oracle.gemm_f32(A, B, 0, 8, threads)
     per_row = max(time.perf_counter() - t0, 1e-3) / 8
@@ -201,15 +209,15 @@ def run_reference(args) -> None:
     for _ in range(args.steps):
         oracle.gemm_f32(A, B, 0, rows, threads)
     dt = (time.perf_counter() - t0) / max(1, args.steps)
-    value = 2.0 * rows * N_DIM * K_DIM / dt / 1e12
+    value = 2.0 * rows * n_dim * k_dim / dt / 1e12
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": "fp16_gemm_8192x8192x8192", "M": ROWS_PER_GPU, "N": N_DIM, "K": K_DIM,
+            "config": {"workload": workload_name(args.workload), "M": m_full, "N": n_dim, "K": k_dim,
                        "step": f"{rows}-row sample of the workload per step"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{rows} of 8192 rows per step (CPU oracle: the reference has no host GEMM)"},
+                             "sample": f"{rows} of {m_full} rows per step (CPU oracle: the reference has no host GEMM)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -398,8 +406,7 @@ def run_b200(args) -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f16", "accumulate": "f32", "data": "synthetic",
-            "config": {"workload": ("fp16_gemm_8192x8192x8192_per_gpu" if args.workload == "gemm8192"
-                                    else "fp16_gemm_32768x32768x32768_row_sharded"),
+            "config": {"workload": workload_name(args.workload),
                        "M": M, "N": N_DIM, "K": K_DIM,
                        "rows_per_gpu": rows, "parallelism": f"row-block x{world} (B replicated)",
                        "layout": "A MxK row-major, B NxK (K contiguous), C MxN row-major",
