@@ -1,0 +1,31 @@
+"""bench.py's reference arm on CPU: one JSON line with the contract's keys, on the same
+workload, metric and unit as the B200 arm."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.mark.parametrize("workload,scaling", [("gemm8192", "weak")])
+def test_reference_arm_json_line(workload, scaling):
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "0", "--workload", workload],
+                          cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [l for l in proc.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e", "impl"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["scaling"] == scaling and d["higher_is_better"] is True
+    assert d["unit"] == "TFLOP/s" and d["value"] > 0
+    assert d["config"]["workload"] == "fp16_gemm_8192x8192x8192_per_gpu"
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
