@@ -282,11 +282,12 @@ def run_b200(args) -> None:
     def step():
         vg.gemm(A, B, out=C, version=version, stream=stream)
 
-    def timed(fn, steps, warmup, sampler=None):
+    def timed(fn, steps, warmup, sampler=None, label="timed"):
         for _ in range(warmup):
             fn()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(f"{label}: {steps} steps")  # marks the region in profiler timelines
         e0.record(stream)
         if sampler:
             sampler.start()
@@ -296,11 +297,12 @@ def run_b200(args) -> None:
         e1.synchronize()
         if sampler:
             sampler.stop()
+        torch.cuda.nvtx.range_pop()
         barrier()
         return e0.elapsed_time(e1) / steps
 
     sampler = ClockSampler(local)
-    ms_local = timed(step, args.steps, max(3, args.warmup), sampler)
+    ms_local = timed(step, args.steps, max(3, args.warmup), sampler, label="b200")
     ms = max_over_ranks(ms_local)
     flop_step = 2.0 * M * N_DIM * K_DIM
     value = flop_step / (ms * 1e-3) / 1e12
@@ -311,9 +313,9 @@ def run_b200(args) -> None:
     def cublas_step():
         vg.cublas_gemm(A, B, out=Cref, stream=stream)
 
-    ms_cublas_1 = max_over_ranks(timed(cublas_step, args.steps, max(3, args.warmup)))
-    ms_again = max_over_ranks(timed(step, args.steps, 3))
-    ms_cublas_2 = max_over_ranks(timed(cublas_step, args.steps, 3))
+    ms_cublas_1 = max_over_ranks(timed(cublas_step, args.steps, max(3, args.warmup), label="cublas"))
+    ms_again = max_over_ranks(timed(step, args.steps, 3, label="b200 repeat"))
+    ms_cublas_2 = max_over_ranks(timed(cublas_step, args.steps, 3, label="cublas repeat"))
     ms_cublas = 0.5 * (ms_cublas_1 + ms_cublas_2)
     ms_pair = 0.5 * (ms + ms_again)
     # Best cuBLASLt algorithm (heuristic sweep) beside this kernel, both timed the same way:

@@ -143,3 +143,18 @@ def test_allgather_plan_never_uses_stream_k(vg):
     import ctypes
     out = (ctypes.c_int * 16)()
     assert vg.lib().vg_b200_plan(-1, 512, 1024, 4096, 256, 256, 256, 3, 148, out) != 0  # no mode 3
+
+
+def test_entry_points_fail_loudly_without_a_gpu(vg):
+    """With no usable GPU every entry point returns a CUDA error code; nothing falls back to
+    a CPU path. (Skipped where a GPU is visible: the pointers here are not device memory.)"""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    L = vg.lib()
+    assert L.vg_b200_gemm_f16(16, 16, 16, 8, 8, 8, None) != 0
+    assert L.vg_b200_gemm_f16_version(2, 16, 16, 16, 8, 8, 8, None) != 0
+    assert L.vg_b200_gemm_f16_noalloc(16, 16, 16, 8, 8, 8, None) != 0
+    assert L.vg_b200_is_available(0) == 0
+    with pytest.raises(vg.VibeGemmError):
+        vg._check(L.vg_b200_gemm_f16(16, 16, 16, 8, 8, 8, None), "vg_b200_gemm_f16")
