@@ -94,11 +94,14 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
     if (K >= 16384 && t3 >= pairs)
         return 6;
     // Full waves of pair tiles: 256×512 (v3, ~6 % more work per pair-cycle than 256×256 at
-    // 8192³) against 256×256 (v2), each charged for its last partial wave.
+    // 8192³) against 256×256 (v2), each charged for its last partial wave. Within 1.5 % v3
+    // wins: it moves a quarter less data, which the estimate does not credit (8191×8193×4099:
+    // estimates 0.9 % apart, v3 measured 7.8 % faster; 4096×14336×4096: 1.9 % apart, v2
+    // 1.8 % faster).
     if (K >= 1024 && t3 >= pairs) {
         const double e3 = (double)((t3 + pairs - 1) / pairs) * 512 / 1.057;
         const double e2 = (double)((t2 + pairs - 1) / pairs) * 256;
-        return e3 <= e2 ? 3 : 2;
+        return e3 <= 1.015 * e2 ? 3 : 2;
     }
     if (t2 >= pairs)
         return 2;
