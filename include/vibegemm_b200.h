@@ -86,7 +86,7 @@ int vg_host_pipeline_gemm_f16(vg_host_pipeline_t pipeline, const void *hA, const
                               vg_stream_t done_stream);
 
 /* Validation build: the same main loop as `version`, fp32 C (no fp16 rounding), so
- * accumulation error can be judged separately from output quantisation. No
+ * accumulation error can be measured separately from output quantisation. No
  * counterpart in the reference (its only check is fp16-vs-cuBLAS,
  * include/utils.cuh:70-118). */
 int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C, int M, int N,
@@ -94,7 +94,7 @@ int vg_b200_gemm_f16_f32out(int version, const void *A, const void *B, float *C,
 
 /* cuBLAS yardstick with the row-major-C operand order.
  * Replaces CublasBackend::run (csrc/cublas_backends.cu:21-35, the HAS_A100 branch
- * :28-31, which writes row-major C) — the reference judge. */
+ * :28-31, which writes row-major C) — the reference engine's arbiter of correctness. */
 int vg_cublas_gemm_f16(const void *A, const void *B, void *C, int M, int N, int K,
                        vg_stream_t stream);
 

@@ -4,7 +4,7 @@
 //  * the naive scalar kernel csrc/a100/gemm_8192x8192_v0.cuh:23-82 (plain CUDA, no
 //    mma.sync) — sequential-k fp32 accumulation, the semantics the oracle restates;
 //  * CublasBackend from csrc/cublas_backends.cu:12-44 with HAS_A100 (the row-major-C
-//    operand order, :28-31) — the reference's judge;
+//    operand order, :28-31) — the reference engine's arbiter of correctness;
 //  * fill_random_fp16 from include/utils.cuh:59-66 on a real device buffer.
 // The reference files are included from the reference tree at build time; nothing
 // is copied into this repository.

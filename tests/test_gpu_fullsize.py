@@ -1,6 +1,6 @@
 """Full-size parity at the BASELINE configurations.
 
-The judge here is the reference's own naive kernel (csrc/a100/gemm_8192x8192_v0.cuh,
+The arbiter here is the reference's own naive kernel (csrc/a100/gemm_8192x8192_v0.cuh,
 compiled for sm_100a into oracle/_ref by `make -C oracle ref`): sequential-k fp32
 accumulation, i.e. exactly the semantics of the CPU oracle (bit-identical to it, checked
 below on sampled rows), but fast enough on the GPU to compare every element of an
@@ -8,7 +8,7 @@ below on sampled rows), but fast enough on the GPU to compare every element of a
 element, plus the CPU oracle on sampled first/last rows. Skipped where oracle/_ref was not
 built (the reference tree is needed at build time).
 
-cuBLAS is not the judge at odd K: with lda = 4099 it fails the reference's check_error
+cuBLAS is not the arbiter at odd K: with lda = 4099 it fails the reference's check_error
 against the oracle (measured on a B200 with cuBLAS 12.9), while every kernel here passes.
 """
 import numpy as np

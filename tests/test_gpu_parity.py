@@ -1,5 +1,5 @@
 """Parity of every B200 kernel version with the oracle (CPU restatement of the reference
-GEMM) and with the reference's judge (cuBLAS), through the C ABI.
+GEMM) and with the reference engine's arbiter (cuBLAS), through the C ABI.
 
 Bars (written here, per the reference's validation):
   * fp16 output: the reference's check_error (|r-c| <= 1e-3 + 1e-2*|r|, include/utils.cuh:70-118)

@@ -109,7 +109,7 @@ def test_gemm_matches_reference_naive_kernel_golden(orc):
         key = f"{M}x{N}x{K}_s{sa}_{sb}"
         mine = orc.gemm_f16(A, B)
         assert np.array_equal(mine, g[key + "_naive"]), key            # bit-exact vs reference v0
-        ok, st = orc.check_error(g[key + "_cublas"], mine)              # the reference's own judge
+        ok, st = orc.check_error(g[key + "_cublas"], mine)              # the reference's own arbiter
         assert ok, (key, st)
 
 
