@@ -623,20 +623,44 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         continue;
                     }
                     if (u.kind == kUnitOwner && epi_ok) {
-                        for (int w2 = u.first_contrib; w2 <= u.last_contrib; ++w2) {
-                            const float *src = slot_of(w2) + row_off;
+                        // Partials of two contributors per round trip (their 32 loads are in
+                        // flight together; reading them one by one was latency-bound), added
+                        // in contributor order.
+                        auto add4 = [](uint32_t *v, const float4 &a) {
+                            v[0] = __float_as_uint(__uint_as_float(v[0]) + a.x);
+                            v[1] = __float_as_uint(__uint_as_float(v[1]) + a.y);
+                            v[2] = __float_as_uint(__uint_as_float(v[2]) + a.z);
+                            v[3] = __float_as_uint(__uint_as_float(v[3]) + a.w);
+                        };
+                        auto ld4 = [&](const float *src, long long quad) {
+                            return *reinterpret_cast<const float4 *>(src + quad * (T::BM * 4));
+                        };
+                        int w2 = u.first_contrib;
+                        for (; w2 + 1 <= u.last_contrib; w2 += 2) {
+                            const float *s0 = slot_of(w2) + row_off;
+                            const float *s1 = slot_of(w2 + 1) + row_off;
+                            float4 a0[8], b0[8], a1[8], b1[8];
 #pragma unroll
                             for (int q = 0; q < 8; ++q) {
-                                const float4 a = *reinterpret_cast<const float4 *>(src + (quad0 + q) * (T::BM * 4));
-                                const float4 b = *reinterpret_cast<const float4 *>(src + (quad0 + 8 + q) * (T::BM * 4));
-                                v0[4 * q] = __float_as_uint(__uint_as_float(v0[4 * q]) + a.x);
-                                v0[4 * q + 1] = __float_as_uint(__uint_as_float(v0[4 * q + 1]) + a.y);
-                                v0[4 * q + 2] = __float_as_uint(__uint_as_float(v0[4 * q + 2]) + a.z);
-                                v0[4 * q + 3] = __float_as_uint(__uint_as_float(v0[4 * q + 3]) + a.w);
-                                v1[4 * q] = __float_as_uint(__uint_as_float(v1[4 * q]) + b.x);
-                                v1[4 * q + 1] = __float_as_uint(__uint_as_float(v1[4 * q + 1]) + b.y);
-                                v1[4 * q + 2] = __float_as_uint(__uint_as_float(v1[4 * q + 2]) + b.z);
-                                v1[4 * q + 3] = __float_as_uint(__uint_as_float(v1[4 * q + 3]) + b.w);
+                                a0[q] = ld4(s0, quad0 + q);
+                                b0[q] = ld4(s0, quad0 + 8 + q);
+                                a1[q] = ld4(s1, quad0 + q);
+                                b1[q] = ld4(s1, quad0 + 8 + q);
+                            }
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                add4(v0 + 4 * q, a0[q]);
+                                add4(v1 + 4 * q, b0[q]);
+                                add4(v0 + 4 * q, a1[q]);
+                                add4(v1 + 4 * q, b1[q]);
+                            }
+                        }
+                        if (w2 <= u.last_contrib) {
+                            const float *s0 = slot_of(w2) + row_off;
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                add4(v0 + 4 * q, ld4(s0, quad0 + q));
+                                add4(v1 + 4 * q, ld4(s0, quad0 + 8 + q));
                             }
                         }
                     }
