@@ -8,9 +8,10 @@
 //               into a STAGES-deep shared-memory ring guarded by full/empty mbarriers.
 //   warp 1      TMEM owner (alloc 512 columns = two 128×256 fp32 accumulators) and,
 //               in the leader CTA, the single-thread tcgen05.mma issuer.
-//   warps 2..5  epilogue: tcgen05.ld (32 lanes × 32 columns) → cvt.rn fp16 →
-//               either 128-B-swizzled smem staging + TMA store (aligned C) or
-//               predicated direct stores (unaligned C / fp32 validation output).
+//   warps 2..   epilogue (4 warps for single CTAs, 8 for CTA pairs): tcgen05.ld
+//               (32 lanes × 32 columns) → cvt.rn fp16 → 128-B-swizzled smem staging,
+//               then a TMA store (aligned C) or coalesced row stores (unaligned C);
+//               predicated direct stores for v0 and the fp32 validation output.
 //
 // CG = 1: one CTA computes a 128×256 tile with tcgen05.mma.cta_group::1 (M=128,N=256).
 // CG = 2: a CTA pair computes a 256×BN tile with tcgen05.mma.cta_group::2 (M=256,
