@@ -29,3 +29,14 @@ def test_reference_arm_json_line(workload, scaling):
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_non_zero_ranks_are_silent():
+    """Under torchrun only rank 0 runs the reference arm; other ranks exit 0 without output."""
+    import os
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2",
+                           "--steps", "1", "--warmup", "0"], cwd=ROOT, env=env, capture_output=True,
+                          text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    assert not [l for l in proc.stdout.splitlines() if l.startswith("{")]
