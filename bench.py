@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--version", type=int, default=None, help="kernel version (default: the per-shape choice of vg_b200_gemm_f16)")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="row blocks per host-pipeline GEMM (uploads, GEMMs and downloads overlap per block)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--allgather", choices=["none", "nccl", "fused", "fused-p2p"], default="none",
                     help="N>1: also time the all-gather of C, as a separate NCCL all-gather after "
@@ -341,7 +343,7 @@ def run_b200(args) -> None:
     hC = torch.empty(C.shape, dtype=C.dtype, pin_memory=True)
     hA.copy_(A)
     hB.copy_(B)
-    pipe = vg.HostPipeline(device=local, chunks=4)
+    pipe = vg.HostPipeline(device=local, chunks=args.e2e_chunks)
 
     def e2e_step():
         pipe.gemm(hA, hB, hC, stream=stream)
@@ -352,8 +354,8 @@ def run_b200(args) -> None:
     e2e = {"value": flop_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": world * (A.numel() + B.numel()) * 2,
            "d2h_bytes_per_step": world * C.numel() * 2, "ms_per_step": ms_e2e,
-           "path": "vg_host_pipeline_gemm_f16 C ABI: pinned host A,B -> HBM in 4 row blocks, "
-                   "GEMM per block, C -> pinned host; steps overlap uploads and downloads"}
+           "path": f"vg_host_pipeline_gemm_f16 C ABI: pinned host A,B -> HBM in {args.e2e_chunks} row "
+                   "blocks, GEMM per block, C -> pinned host; steps overlap uploads and downloads"}
 
     allgather = None
     if args.allgather == "nccl" and world > 1:
