@@ -11,11 +11,17 @@ A step is one C = A·B^T GEMM (fp16 in, fp32 accumulate, fp16 out) of the worklo
 * ``--workload sharded32k``: one M=N=K=32768 GEMM split into N contiguous row blocks of A
   and C, B replicated (strong scaling; ``--allgather`` also times the NCCL all-gather of C).
 
+With the default workload the line also carries ``sharded32k``: the 32768³ row-sharded GEMM
+at the same N (GEMM-only ms and TFLOP/s, max over ranks, and the fraction of N × the measured
+peak), and at N > 1 the same GEMM with the all-gather of C fused into its epilogue over NVLink
+(``gathered_rows_exact`` checks every rank's gathered rows) beside GEMM + NCCL all-gather.
+
 Rank 0 prints ONE JSON line.
 
 * ``value``      whole-job TFLOP/s, inputs resident in HBM, CUDA events on the launching
                  stream around exactly K launches, barrier + synchronize on both sides,
-                 max over ranks. A+B+C = 384 MiB per GPU per step > 126 MB L2.
+                 max over ranks (``timed``: no host work between the events but the
+                 launches). A+B+C = 384 MiB per GPU per step > 126 MB L2.
 * ``e2e``        the same metric through the C ABI with pinned HOST buffers: every step
                  copies A and B host→device, runs the GEMM and copies C device→host.
 * ``cublas``     cublasGemmEx on the same buffers in the same run (the yardstick).
@@ -77,6 +83,9 @@ def parse_args():
                          "the GEMM (nccl) or fused into the GEMM kernel's epilogue over NVLink "
                          "(fused: NVLink multicast when available; fused-p2p: one store per peer)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm8192")
+    ap.add_argument("--sharded-steps", type=int, default=10,
+                    help="timed steps of the 32768^3 row-sharded record added to the line "
+                         "(0 leaves it out)")
     return ap.parse_args()
 
 
@@ -98,17 +107,24 @@ def profile_traffic() -> float | None:
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+    """Samples the SM clock and clock-event reasons through NVML on a background thread.
+
+    ``start`` only starts the thread (every NVML query runs on it, none on the caller's
+    thread), so it is called once before the first warm-up; ``enter`` / ``leave`` only flip
+    a flag that tags the samples taken inside a timed region. The summary is the median SM
+    clock of the tagged samples and every reason seen in them.
+    """
 
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, cuda_index: int, period_s: float = 0.005):
-        self.samples: list[tuple[int, int]] = []
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
+        self.samples: list[tuple[int, int, bool]] = []  # (MHz, reason bits, inside a timed region)
         self.max_mhz = None
         self.period = period_s
+        self.in_region = False
         self._stop = threading.Event()
         self._thread = None
         self.h = None
@@ -135,8 +151,10 @@ class ClockSampler:
         try:
             get_reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
-            self.samples.append((self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
-                                 int(get_reasons(self.h))))
+            tagged = self.in_region
+            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            bits = int(get_reasons(self.h))
+            self.samples.append((mhz, bits, tagged and self.in_region))
         except Exception:
             pass
 
@@ -146,27 +164,74 @@ class ClockSampler:
             time.sleep(self.period)
 
     def start(self):
-        if self.h is not None:
-            self._sample()
+        """Starts the sampling thread; call it before the warm-up, never inside a timed region."""
+        if self.h is not None and self._thread is None:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
+
+    def enter(self):
+        self.in_region = True
+
+    def leave(self):
+        self.in_region = False
 
     def stop(self):
         if self._thread:
             self._stop.set()
             self._thread.join()
-            self._sample()
+            self._thread = None
 
     def summary(self) -> dict:
         if self.h is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
-        mhz = [s[0] for s in self.samples]
+        tagged = [s for s in self.samples if s[2]]
+        use = tagged or self.samples
+        mhz = [s[0] for s in use]
         bits = 0
-        for _, r in self.samples:
-            bits |= r
+        for s in use:
+            bits |= s[1]
         reasons = [name for b, name in self.REASONS.items() if bits & b and name != "gpu_idle"]
         return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(mhz)}
+                "reasons": reasons, "samples": len(mhz),
+                "window": "inside the timed regions" if tagged else "whole run"}
+
+
+# Device-side lead before each timed region: the GPU spins this many cycles (about 2 ms at
+# the B200's 1965 MHz boost clock) while the host enqueues the start event and the first
+# launches, so neither the host's launch cost nor a host hiccup at the start lands between
+# the two events.
+LEAD_CYCLES = 4_000_000
+
+
+def timed(fn, steps: int, warmup: int, stream, barrier, sampler=None, label: str = "timed") -> float:
+    """Mean device milliseconds per call of `fn` over `steps` calls, CUDA events on `stream`.
+
+    Order: `warmup` untimed calls, barrier (+ synchronize), sampler tag on, a device-side lead
+    (LEAD_CYCLES), start event, exactly `steps` calls, end event, wait for it, sampler tag off,
+    barrier. Nothing but the calls themselves is enqueued or run on this thread between the
+    two events; the clock sampler's NVML queries run on its own thread.
+    """
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.enter()
+    torch.cuda.nvtx.range_push(f"{label}: {steps} steps")  # marks the region in profiler timelines
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(LEAD_CYCLES)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    torch.cuda.nvtx.range_pop()
+    if sampler:
+        sampler.leave()
+    barrier()
+    return e0.elapsed_time(e1) / steps
 
 
 def cpu_baseline(seconds: float, N_DIM: int = N_DIM, K_DIM: int = K_DIM) -> dict:
@@ -284,27 +349,15 @@ def run_b200(args) -> None:
     def step():
         vg.gemm(A, B, out=C, version=version, stream=stream)
 
-    def timed(fn, steps, warmup, sampler=None, label="timed"):
-        for _ in range(warmup):
-            fn()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.nvtx.range_push(f"{label}: {steps} steps")  # marks the region in profiler timelines
-        e0.record(stream)
-        if sampler:
-            sampler.start()
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        e1.synchronize()
-        if sampler:
-            sampler.stop()
-        torch.cuda.nvtx.range_pop()
-        barrier()
-        return e0.elapsed_time(e1) / steps
-
+    # The clock sampler runs on its own thread from before the first warm-up to the end of the
+    # last GEMM block; the timed regions only tag its samples.
     sampler = ClockSampler(local)
-    ms_local = timed(step, args.steps, max(3, args.warmup), sampler, label="b200")
+    sampler.start()
+
+    def run_timed(fn, steps, warmup, label, sample=True):
+        return timed(fn, steps, warmup, stream, barrier, sampler if sample else None, label)
+
+    ms_local = run_timed(step, args.steps, max(3, args.warmup), "b200")
     ms = max_over_ranks(ms_local)
     flop_step = 2.0 * M * N_DIM * K_DIM
     value = flop_step / (ms * 1e-3) / 1e12
@@ -315,16 +368,16 @@ def run_b200(args) -> None:
     def cublas_step():
         vg.cublas_gemm(A, B, out=Cref, stream=stream)
 
-    ms_cublas_1 = max_over_ranks(timed(cublas_step, args.steps, max(3, args.warmup), label="cublas"))
-    ms_again = max_over_ranks(timed(step, args.steps, 3, label="b200 repeat"))
-    ms_cublas_2 = max_over_ranks(timed(cublas_step, args.steps, 3, label="cublas repeat"))
+    ms_cublas_1 = max_over_ranks(run_timed(cublas_step, args.steps, max(3, args.warmup), "cublas"))
+    ms_again = max_over_ranks(run_timed(step, args.steps, 3, "b200 repeat"))
+    ms_cublas_2 = max_over_ranks(run_timed(cublas_step, args.steps, 3, "cublas repeat"))
     ms_cublas = 0.5 * (ms_cublas_1 + ms_cublas_2)
     ms_pair = 0.5 * (ms + ms_again)
     # Best cuBLASLt algorithm (heuristic sweep) beside this kernel, both timed the same way:
     # short bursts (3 warm-up + 10 launches) right after one another.
     lt_ms = [m for m in vg.cublaslt_sweep(A, B, out=Cref, max_algos=16, warmup=3, iters=10,
                                           stream=stream) if m > 0]
-    ms_burst = timed(step, 10, 3)
+    ms_burst = run_timed(step, 10, 3, "b200 burst")
     lt_best = max_over_ranks(min(lt_ms) if lt_ms else 1e30)  # every rank takes part
     lt_best = None if lt_best >= 1e30 else lt_best
     ms_burst = max_over_ranks(ms_burst)
@@ -349,7 +402,7 @@ def run_b200(args) -> None:
         pipe.gemm(hA, hB, hC, stream=stream)
 
     e2e_steps = max(1, min(args.steps, args.e2e_steps if args.workload == "gemm8192" else 2))
-    ms_e2e = max_over_ranks(timed(e2e_step, e2e_steps, 3))
+    ms_e2e = max_over_ranks(run_timed(e2e_step, e2e_steps, 3, "e2e", sample=False))
     pipe.close()
     e2e = {"value": flop_step / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": world * (A.numel() + B.numel()) * 2,
@@ -361,7 +414,7 @@ def run_b200(args) -> None:
     if args.allgather == "nccl" and world > 1:
         def gather_step():
             sh.gather(C)
-        ms_ag = max_over_ranks(timed(gather_step, min(args.steps, 20), 3))
+        ms_ag = max_over_ranks(run_timed(gather_step, min(args.steps, 20), 3, "nccl all-gather", sample=False))
         allgather = {"mode": "nccl", "ms_per_step": ms_ag, "bytes_gathered": M * N_DIM * 2,
                      "gemm_plus_allgather_value": flop_step / ((ms + ms_ag) * 1e-3) / 1e12,
                      "note": "NCCL all_gather_into_tensor of the row-major C shards, timed after the GEMM"}
@@ -372,7 +425,7 @@ def run_b200(args) -> None:
         def fused_step():
             fused.run(A, B, stream=stream)
 
-        ms_fused = max_over_ranks(timed(fused_step, args.steps, 3))
+        ms_fused = max_over_ranks(run_timed(fused_step, args.steps, 3, "fused all-gather", sample=False))
         fused.barrier()
         # Check: the rows gathered from the next rank equal that rank's GEMM, recomputed here
         # from the same seeded generator.
@@ -394,6 +447,86 @@ def run_b200(args) -> None:
         del fused
 
     pk = peaks()
+
+    def sharded32k_record() -> dict:
+        """The north star's scaling config beside the weak-scaling headline: ONE M=N=K=32768
+        GEMM split into `world` contiguous row blocks of A and C, B replicated (strong
+        scaling). GEMM-only time (max over ranks), and at N > 1 the same GEMM with the
+        all-gather of C fused into its epilogue (NVLink multicast when the node has it) and,
+        for comparison, the GEMM's C shards gathered afterwards by NCCL."""
+        from vibegemm_b200.mgpu import FusedAllGatherGemm
+        M32 = N32 = K32 = 32768
+        sh32 = RowShardedGemm(M32, N32, K32, rank, world)
+        p0, prow = sh32.local
+        g = torch.Generator(device="cuda")
+        g.manual_seed(4242 + rank)
+        A32 = torch.empty((prow, K32), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+        g.manual_seed(7777)
+        B32 = torch.empty((N32, K32), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+        C32 = torch.empty((prow, N32), dtype=torch.float16, device="cuda")
+        v32 = vg.plan(-1, prow, N32, K32, A32.data_ptr(), B32.data_ptr(), C32.data_ptr())["version"]
+        steps32 = max(1, args.sharded_steps)
+
+        def gemm32():
+            vg.gemm(A32, B32, out=C32, stream=stream)
+
+        flop32 = 2.0 * M32 * N32 * K32
+        ms32 = max_over_ranks(run_timed(gemm32, steps32, 3, "sharded32k gemm"))
+        tf32 = flop32 / (ms32 * 1e-3) / 1e12
+        rec = {"workload": workload_name("sharded32k"), "M": M32, "N": N32, "K": K32,
+               "rows_per_gpu": prow, "n_gpus": world, "scaling": "strong", "steps": steps32,
+               "kernel": vg.version_name(v32) + " (via vg_b200_gemm_f16, per-shape choice)",
+               "gemm_ms": ms32, "gemm_tflops": tf32, "per_gpu_tflops": tf32 / world,
+               "frac_of_n_peak": tf32 / (world * pk["tflops"]),
+               "peak_per_gpu": pk["tflops"], "inputs": "uniform[-1,1] fp16, seeded device generator"}
+        if world > 1:
+            fused = FusedAllGatherGemm(M32, N32, K32, rank, world, multicast=True)
+
+            def fused32():
+                fused.run(A32, B32, stream=stream)
+
+            ms_f = max_over_ranks(run_timed(fused32, steps32, 3, "sharded32k fused all-gather"))
+            fused.barrier()
+            # Every rank's full C: its own rows equal the GEMM-only output, and the next rank's
+            # rows equal that rank's GEMM recomputed here from the same seeded generator (the
+            # same kernel version: bit for bit).
+            own_ok = bool(torch.equal(fused.C[p0:p0 + prow], C32))
+            peer = (rank + 1) % world
+            q0, qrow = RowShardedGemm(M32, N32, K32, peer, world).local
+            g.manual_seed(4242 + peer)
+            A_peer = torch.empty((qrow, K32), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+            v_fused = vg.plan(-1, qrow, N32, K32, 256, 256, 256, allgather=True)["version"]
+            want = vg.gemm(A_peer, B32, version=v_fused, stream=stream)
+            torch.cuda.synchronize()
+            peer_ok = bool(torch.equal(fused.C[q0:q0 + qrow], want))
+            exact = max_over_ranks(0.0 if (own_ok and peer_ok) else 1.0) == 0.0
+            mode = "fused-multicast" if fused.c_multicast_ptr else "fused-p2p"
+            fused.barrier()
+            del fused, A_peer, want
+
+            def nccl32():
+                sh32.gather(C32)
+
+            ms_n = max_over_ranks(run_timed(nccl32, steps32, 3, "sharded32k nccl all-gather", sample=False))
+            rec["allgather"] = {
+                "mode": mode, "gemm_plus_allgather_ms": ms_f,
+                "gemm_plus_allgather_tflops": flop32 / (ms_f * 1e-3) / 1e12,
+                "allgather_hidden": ms_f <= 1.02 * ms32,
+                "gathered_rows_exact": exact,
+                "bytes_gathered": M32 * N32 * 2,
+                "nccl_allgather_after_gemm_ms": ms_n,
+                "gemm_then_nccl_tflops": flop32 / ((ms32 + ms_n) * 1e-3) / 1e12,
+                "note": "fused: one kernel per rank whose epilogue stores every C tile into every "
+                        "rank's full C over NVLink; nccl: all_gather_into_tensor of the C shards "
+                        "after the GEMM, timed alone"}
+        del A32, B32, C32
+        torch.cuda.empty_cache()
+        return rec
+
+    sharded = None
+    if args.workload == "gemm8192" and args.sharded_steps > 0:
+        sharded = sharded32k_record()
+    sampler.stop()
     per_gpu_launch_tflops = 2.0 * rows * N_DIM * K_DIM / (ms_local * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": per_gpu_launch_tflops, "peak": pk["tflops"], "unit": UNIT,
             "frac": per_gpu_launch_tflops / pk["tflops"], "traffic": profile_traffic(),
@@ -443,6 +576,8 @@ def run_b200(args) -> None:
         }
         if allgather:
             line["allgather"] = allgather
+        if sharded:
+            line["sharded32k"] = sharded
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

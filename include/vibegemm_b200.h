@@ -50,14 +50,20 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
  * (needed when K % 8 != 0 or A/B is not 16-byte aligned) from the CUDA stream-ordered
  * pool; this entry point uses a fixed 32 MiB array in the library's device memory
  * instead and never calls cudaMalloc, cudaMallocAsync, cudaFree or an allocating library.
- *   - Limit: the call's workspace must fit in 32 MiB: the padded copies
- *     (M + N) * roundup(K, 8) * 2 bytes, plus for small grids that use stream-K scheduling
- *     the fp32 partial tiles (at most 148 * 128 KB = 18.5 MiB). Larger workspaces return
+ *   - Limit: the call's workspace must fit in 32 MiB: a padded copy of each operand that
+ *     needs one (M * roundup(K, 8) * 2 bytes for A, N * roundup(K, 8) * 2 bytes for B), plus
+ *     for small grids that use stream-K scheduling the fp32 partial tiles and their flags
+ *     (at most 148 * 128 KB = 18.5 MiB). Larger workspaces return
  *     VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing. Problems that need neither have
  *     no size limit.
- *   - The 32 MiB are held on every GPU that loads the library until the process exits.
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - The 32 MiB belong to the library's device code. With CUDA's lazy module loading
+ *     (the default) a GPU reserves them when that code is first loaded on it, i.e. at the
+ *     first GEMM call of any entry point on that device, and holds them until the process
+ *     exits. A host that gives all of a GPU's memory to its own pool must make one call on
+ *     that device first.
+ *   - The first call of this entry point on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture. A failed
+ *     lookup is returned as that call's error and retried by the next call.
  *   - All calls share the array: calls that overlap on the GPU (different streams, or
  *     different host threads on one device) race on it; serialise them. Each call
  *     rewrites every scratch byte it reads and zeroes its stream-K flags itself
@@ -156,7 +162,9 @@ int vg_b200_selftest_wait_timeout(unsigned long long timeout_ns);
  * once with multimem stores and the switch delivers it to every rank; otherwise one store
  * per peer. The all-gather's traffic overlaps the math tile by tile. No kernel waits on
  * another GPU: after the call, the ranks must synchronise (e.g. a barrier) before reading
- * rows written by peers. Returns 0 or a cudaError_t code. */
+ * rows written by peers. K must be positive (K == 0, an all-zero C, is rejected with
+ * cudaErrorInvalidValue rather than leaving the peers' rows stale). Returns 0 or a
+ * cudaError_t code. */
 int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks,
                                void *C_multicast, int world, int rank, long long row0, int M_local,
                                int N, int K, vg_stream_t stream);

@@ -4,7 +4,7 @@ Each rank computes its row block of C with vg_b200_gemm_f16_allgather, whose epi
 writes the rows into the other rank's full C over NVLink — one store per peer, or one
 NVLink-multicast (multimem) store when the node supports NVLS; after a barrier every rank's
 full C must equal a single-GPU GEMM of the whole problem with the same kernel version, bit
-for bit.
+for bit, and pass the reference's check_error against the CPU oracle.
 """
 import os
 import socket
@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, N, K, multicast, q):
+def _worker(rank, world, port, M, N, K, multicast, side_stream, q):
     import sys
     from datetime import timedelta
     from pathlib import Path
@@ -42,8 +42,12 @@ def _worker(rank, world, port, M, N, K, multicast, q):
         r0, rows = fused.sh.local
         dA = torch.from_numpy(A[r0:r0 + rows].view(np.int16).copy()).cuda().view(torch.float16)
         dB = torch.from_numpy(B.view(np.int16).copy()).cuda().view(torch.float16)
-        for _ in range(2):  # twice: repeated launches into the same buffers
-            fused.run(dA, dB)
+        # Twice: repeated launches into the same buffers. On a side stream, the barrier must
+        # still order every rank's kernel (it synchronises the device before the collective).
+        s = torch.cuda.Stream() if side_stream else torch.cuda.current_stream()
+        s.wait_stream(torch.cuda.current_stream())
+        for _ in range(2):
+            fused.run(dA, dB, stream=s)
         fused.barrier()
         # Reference: the whole problem on this GPU with the version the shards resolved to.
         # Every version except stream-K keeps one accumulation chain per output and agrees
@@ -52,16 +56,22 @@ def _worker(rank, world, port, M, N, K, multicast, q):
         full = vg.gemm(torch.from_numpy(A.view(np.int16).copy()).cuda().view(torch.float16), dB,
                        version=v)
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(fused.C, full)), vg.device_status(), bool(fused.c_multicast_ptr)))
+        got = fused.C.cpu().view(torch.int16).numpy().view(np.uint16)
+        # And against the CPU oracle (the reference's naive GEMM restated), with the reference
+        # engine's check_error: an error common to both GPU launches would not pass this.
+        ok_oracle, st = oracle.check_error(oracle.gemm_f16(A, B), got)
+        q.put((rank, bool(torch.equal(fused.C, full)), vg.device_status(), bool(fused.c_multicast_ptr),
+               bool(ok_oracle), str(st)))
         fused.barrier()
         del fused
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("side_stream", [False, True], ids=["current_stream", "side_stream"])
 @pytest.mark.parametrize("multicast", [False, True], ids=["p2p", "nvls"])
 @pytest.mark.parametrize("M,N,K", [(1536, 2048, 1024), (1001, 1024, 4099)])
-def test_fused_gemm_allgather_two_gpus(M, N, K, multicast):
+def test_fused_gemm_allgather_two_gpus(M, N, K, multicast, side_stream):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -70,7 +80,8 @@ def test_fused_gemm_allgather_two_gpus(M, N, K, multicast):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, multicast, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, multicast, side_stream, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -82,5 +93,6 @@ def test_fused_gemm_allgather_two_gpus(M, N, K, multicast):
     res = sorted(q.get(timeout=10) for _ in range(world))
     assert [r[1] for r in res] == [True, True], res
     assert [r[2] for r in res] == [0, 0], res
+    assert [r[4] for r in res] == [True, True], res  # each rank's full C vs the oracle
     if multicast and not res[0][3]:
         pytest.skip("no NVLink multicast on this node (per-peer path was checked)")

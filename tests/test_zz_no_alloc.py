@@ -87,3 +87,35 @@ def test_noalloc_needs_no_scratch_when_aligned(vg, orc):
     A, B = orc.make_inputs(1024, 2048, 512)
     ref, new = _run_both(vg, orc, A, B)
     assert np.array_equal(ref, new)
+
+
+def test_noalloc_stream_k_partials_live_in_the_array(vg, orc):
+    """A grid too small for one wave with long K: the per-shape choice is stream-K (v4), whose
+    fp32 partial tiles and ready flags then sit in the fixed array instead of the pool. Two
+    calls in a row (the second finds the first one's partials and flags still there) must
+    both equal the default entry point bit for bit (same kernel, same contributor order),
+    and the result meets the long-K bound against the fp64 product on sampled rows."""
+    import torch
+    f_noalloc, f_default = _c_abi(vg)
+    M, N, K = 256, 2048, 16384
+    p = vg.plan(-1, M, N, K, 256, 256, 256)
+    assert p["stream_k"] == 1 and p["pad_a"] == 0 and p["pad_b"] == 0, p
+    A, B = orc.make_inputs(M, N, K)
+    dA, dB = to_dev(A), to_dev(B)
+    s = torch.cuda.current_stream().cuda_stream
+    ref = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+    assert f_default(dA.data_ptr(), dB.data_ptr(), ref.data_ptr(), M, N, K, s) == 0
+    outs = []
+    for _ in range(2):
+        C = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        assert f_noalloc(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K, s) == 0
+        outs.append(C)
+    torch.cuda.synchronize()
+    for C in outs:
+        assert torch.equal(C, ref)
+    rows = [0, 1, 129, M - 1]
+    exact = np.concatenate([orc.gemm_f64(A, B, r, 1) for r in rows])
+    got = outs[1].cpu().numpy()[rows].astype(np.float64)
+    bound = 2e-2 * np.sqrt(K / 1024.0)
+    assert np.all(np.abs(got - exact) <= bound + 1e-2 * np.abs(exact))
+    assert vg.device_status() == 0

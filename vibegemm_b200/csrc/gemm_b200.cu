@@ -574,31 +574,39 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 }
 
 // ── workspaces ───────────────────────────────────────────────────────────────
-// Pad workspace of vg_b200_gemm_f16_noalloc: a fixed array in the module's device
-// memory instead of the stream-ordered pool. Every GPU that loads this library holds
-// these kNoAllocScratchBytes until the process exits. In host code the name
-// `noalloc_scratch` is only a host-side stand-in for the symbol; its device address
-// comes from cudaGetSymbolAddress, taken once per device with that device current.
+// Workspace of vg_b200_gemm_f16_noalloc (K-padded operands, stream-K partials and flags):
+// a fixed array in the module's device memory instead of the stream-ordered pool. A GPU
+// reserves these kNoAllocScratchBytes when this module is first loaded on it (with lazy
+// module loading: the first GEMM call on that device) and holds them until the process
+// exits. In host code the name `noalloc_scratch` is only a host-side stand-in for the
+// symbol; its device address comes from cudaGetSymbolAddress, looked up per device with
+// that device current.
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
 static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
 
-struct ScratchAddr {
-    void *ptr = nullptr;
-    cudaError_t err = cudaSuccess;
-};
-ScratchAddr g_scratch[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
+// Device address of the array on device `dev` (current). A successful lookup is kept; a
+// failed one is returned to the caller and tried again on the next call.
+std::atomic<void *> g_scratch[kMaxDevices];
+std::mutex g_scratch_mu;
 
-const ScratchAddr &noalloc_scratch_addr(int dev) {
-    std::call_once(g_scratch_once[dev], [dev] {
-        ScratchAddr &s = g_scratch[dev];
-        s.err = cudaGetSymbolAddress(&s.ptr, noalloc_scratch);
-        if (s.err != cudaSuccess) {
-            s.ptr = nullptr;
-            (void)cudaGetLastError();
-        }
-    });
-    return g_scratch[dev];
+cudaError_t noalloc_scratch_addr(int dev, void *&out) {
+    out = g_scratch[dev].load(std::memory_order_acquire);
+    if (out)
+        return cudaSuccess;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    out = g_scratch[dev].load(std::memory_order_acquire);
+    if (out)
+        return cudaSuccess;
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+        (void)cudaGetLastError();
+        out = nullptr;
+        return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    }
+    g_scratch[dev].store(p, std::memory_order_release);
+    out = p;
+    return cudaSuccess;
 }
 
 // Where a call's workspace (K-padded operands, stream-K partials and flags) lives: the
@@ -677,10 +685,11 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
                 return e;
             base = static_cast<char *>(owned);
         } else {
-            const ScratchAddr &sc = noalloc_scratch_addr(dev);
-            if (sc.err != cudaSuccess)
-                return sc.err;
-            base = static_cast<char *>(sc.ptr);
+            void *sc = nullptr;
+            e = noalloc_scratch_addr(dev, sc);
+            if (e != cudaSuccess)
+                return e;
+            base = static_cast<char *>(sc);
         }
         __half *wa = reinterpret_cast<__half *>(base + wl.a_off);
         __half *wb = reinterpret_cast<__half *>(base + wl.b_off);
@@ -789,8 +798,10 @@ int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N
 int vg_b200_gemm_f16_allgather(const void *A_local, const void *B, void *const *C_ranks,
                                void *C_multicast, int world, int rank, long long row0, int M_local,
                                int N, int K, vg_stream_t stream) {
+    // K == 0 would only zero the local rows (the kernel, which also writes the peers' rows,
+    // never runs), so it is rejected instead of leaving the other ranks' copies stale.
     if (!C_ranks || world < 1 || world > vg::kMaxPeers + 1 || rank < 0 || rank >= world || row0 < 0 ||
-        M_local < 0 || N < 0)
+        M_local < 0 || N < 0 || K <= 0)
         return (int)cudaErrorInvalidValue;
     const size_t off = (size_t)row0 * (size_t)N * sizeof(__half);
     void *peers[vg::kMaxPeers];

@@ -109,7 +109,13 @@ class FusedAllGatherGemm:
                               self.c_multicast_ptr)
 
     def barrier(self) -> None:
+        """Every rank's fused kernels (on any stream) have finished, so every rank's full C
+        holds all rows. This device is synchronised BEFORE the process-group barrier: a
+        barrier's own collective orders only the current stream (and a gloo barrier no GPU
+        work at all), so a rank whose kernel ran on another stream could otherwise pass it
+        while its peer stores are still landing."""
         import torch
         import torch.distributed as dist
+        torch.cuda.synchronize()
         dist.barrier(group=self.group)
         torch.cuda.synchronize()
