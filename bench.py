@@ -121,10 +121,11 @@ class ClockSampler:
                0x100: "display_clock_setting"}
 
     def __init__(self, cuda_index: int, period_s: float = 0.002):
-        self.samples: list[tuple[int, int, bool]] = []  # (MHz, reason bits, inside a timed region)
+        # (MHz, reason bits, label of the timed region the sample fell in, or None)
+        self.samples: list[tuple[int, int, str | None]] = []
         self.max_mhz = None
         self.period = period_s
-        self.in_region = False
+        self.region = None
         self._stop = threading.Event()
         self._thread = None
         self.h = None
@@ -151,10 +152,10 @@ class ClockSampler:
         try:
             get_reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
-            tagged = self.in_region
+            region = self.region
             mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
             bits = int(get_reasons(self.h))
-            self.samples.append((mhz, bits, tagged and self.in_region))
+            self.samples.append((mhz, bits, region if region == self.region else None))
         except Exception:
             pass
 
@@ -169,11 +170,11 @@ class ClockSampler:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
 
-    def enter(self):
-        self.in_region = True
+    def enter(self, label: str = "timed"):
+        self.region = label
 
     def leave(self):
-        self.in_region = False
+        self.region = None
 
     def stop(self):
         if self._thread:
@@ -181,19 +182,30 @@ class ClockSampler:
             self._thread.join()
             self._thread = None
 
-    def summary(self) -> dict:
-        if self.h is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
-        tagged = [s for s in self.samples if s[2]]
-        use = tagged or self.samples
+    def _stats(self, use) -> tuple:
         mhz = [s[0] for s in use]
         bits = 0
         for s in use:
             bits |= s[1]
         reasons = [name for b, name in self.REASONS.items() if bits & b and name != "gpu_idle"]
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(mhz),
-                "window": "inside the timed regions" if tagged else "whole run"}
+        return (statistics.median(mhz) if mhz else None), reasons, len(mhz)
+
+    def summary(self, label: str | None = None) -> dict:
+        """Clocks of the timed region `label` (all timed regions if None), plus the median of
+        every other timed region for comparison."""
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        tagged = [s for s in self.samples if s[2] is not None]
+        mine = [s for s in tagged if label is None or s[2] == label]
+        use = mine or tagged or self.samples
+        mhz, reasons, n = self._stats(use)
+        out = {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": n,
+               "window": (f"timed region '{label}'" if mine and label else
+                          "inside the timed regions" if tagged else "whole run")}
+        labels = sorted({s[2] for s in tagged})
+        if len(labels) > 1:
+            out["by_region"] = {lb: self._stats([s for s in tagged if s[2] == lb])[0] for lb in labels}
+        return out
 
 
 # Device-side lead before each timed region: the GPU spins this many cycles (about 2 ms at
@@ -218,7 +230,7 @@ def timed(fn, steps: int, warmup: int, stream, barrier, sampler=None, label: str
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler:
-        sampler.enter()
+        sampler.enter(label)
     torch.cuda.nvtx.range_push(f"{label}: {steps} steps")  # marks the region in profiler timelines
     with torch.cuda.stream(stream):
         torch.cuda._sleep(LEAD_CYCLES)
@@ -543,7 +555,7 @@ def run_b200(args) -> None:
     if rank == 0 and world == 1:
         cpu = cpu_baseline(args.cpu_seconds, N_DIM, K_DIM)
 
-    clocks = sampler.summary()
+    clocks = sampler.summary("b200")
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

@@ -53,7 +53,7 @@ class _FakeSampler:
     def start(self):
         self.log.append("sampler start")
 
-    def enter(self):
+    def enter(self, label="timed"):
         self.log.append("enter")
 
     def leave(self):
@@ -86,14 +86,14 @@ def test_sampler_tagging_makes_no_nvml_query():
             return 0x4
 
     s = bench.ClockSampler.__new__(bench.ClockSampler)
-    s.samples, s.max_mhz, s.period, s.in_region = [], 1965, 0.001, False
+    s.samples, s.max_mhz, s.period, s.region = [], 1965, 0.001, None
     s.nv, s.h = FakeNV(), object()
     import threading
     s._stop, s._thread = threading.Event(), None
     s.enter()
     s.leave()
     assert calls == []  # the timed region's own thread never talks to NVML
-    s.enter()
+    s.enter("b200")
     s.start()
     import time
     t0 = time.time()
@@ -101,9 +101,9 @@ def test_sampler_tagging_makes_no_nvml_query():
         time.sleep(0.005)
     s.leave()
     s.stop()
-    summ = s.summary()
+    summ = s.summary("b200")
     assert summ["sm_mhz"] == 1965 and summ["reasons"] == ["sw_power_cap"]
-    assert summ["window"] == "inside the timed regions"
+    assert summ["window"] == "timed region 'b200'"
 
 
 def test_run_b200_starts_the_sampler_before_its_first_timed_block():
