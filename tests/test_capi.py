@@ -29,7 +29,8 @@ def test_library_exports_every_declared_symbol(vg):
 def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
-                             "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8"]
+                             "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
+                             "VibeGEMM B200 v9"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -80,9 +81,10 @@ def test_plan_aligned_square(vg):
 
 
 @pytest.mark.parametrize("shape,want", [
-    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 6),
+    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 9),
     ((4096, 14336, 4096), 2),    # 448 256x512 tiles = 6.05 waves; 896 256x256 tiles waste less
-    ((16384, 16384, 16384), 6), ((4096, 32768, 32768), 6),
+    ((16384, 16384, 16384), 9), ((4096, 32768, 32768), 9),   # long K: run-time tiles + chunks
+    ((8192, 8192, 12288), 3),    # below the promotion threshold: one chain per output
     ((4096, 4096, 14336), 3),
     ((8191, 8193, 4099), 3),     # 7.4 vs 14.3 waves: estimates within 1.5 %, v3's data saving wins
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
@@ -90,7 +92,9 @@ def test_plan_aligned_square(vg):
     ((1000, 3000, 8192), 7),     # same tiles, long K: the fifth stage pays
     ((512, 512, 512), 5),
     ((256, 2048, 32768), 4),     # 8 pair tiles, 512 k-blocks each: stream-K over 74 pairs
-    ((512, 8192, 32768), 2),     # 64 pair tiles on 74 pairs: one wave of v2 beats stream-K
+    ((512, 8192, 32768), 8),     # 64 pair tiles on 74 pairs: v2's tile, chunked accumulation
+    ((1000, 3000, 32768), 8),    # long K on an under-filled grid: chains split (v8, not v7)
+    ((512, 8192, 16384), 8), ((512, 8192, 8192), 2),
     ((1000, 3000, 32), 5),
 ])
 def test_auto_version_choice(vg, shape, want):
@@ -118,6 +122,22 @@ def test_plan_tails_and_alignment(vg):
     assert vg.plan(2, 512, 512, 512, 256, 256, 256, f32_out=True)["epilogue"] == "direct_f32"
 
 
+def test_plan_of_run_time_tiles_and_chunks(vg):
+    """v9: persistent 256x512 pairs claiming tiles at run time; K >= 16384 is summed in
+    chunks of 128 k-blocks (K = 8192) up to 768 k-blocks, 64 beyond; below, one chunk."""
+    p = vg.plan(9, 32768, 32768, 32768, 256, 256, 256)
+    assert (p["dyn"], p["promote"], p["promote_kb"], p["num_kb"]) == (1, 1, 128, 512)
+    assert p["grid"] == 148 and p["persistent"] == 1 and p["tile_n"] == 512
+    assert vg.plan(9, 8192, 8192, 8192, 256, 256, 256)["promote_kb"] == 128  # one chunk of 128
+    assert vg.plan(9, 8192, 8192, 65536, 256, 256, 256)["promote_kb"] == 64
+    assert vg.plan(8, 8192, 8192, 8192, 256, 256, 256)["promote_kb"] == 64
+    assert vg.plan(3, 8192, 8192, 8192, 256, 256, 256)["dyn"] == 0
+    # the fused all-gather's choice for a long-K shard promotes too
+    p = vg.plan(-1, 4096, 32768, 32768, 256, 256, 256, allgather=True)
+    assert p["version"] == 9 and p["epilogue"] == "tma_f16_peers"
+    assert vg.plan(-1, 512, 8192, 32768, 256, 256, 256, allgather=True)["version"] == 8
+
+
 def test_plan_rejects_bad_input(vg):
     with pytest.raises(vg.VibeGemmError):
         vg.plan(len(vg.versions()), 16, 16, 16)
@@ -141,7 +161,7 @@ def test_allgather_plan_never_uses_stream_k(vg):
     with pytest.raises(vg.VibeGemmError):
         vg.plan(4, 501, 1024, 4099, 256, 256, 256, allgather=True)
     import ctypes
-    out = (ctypes.c_int * 16)()
+    out = (ctypes.c_int * 18)()
     assert vg.lib().vg_b200_plan(-1, 512, 1024, 4096, 256, 256, 256, 3, 148, out) != 0  # no mode 3
 
 

@@ -17,7 +17,7 @@ from conftest import to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
-VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, -1]  # -1: the default entry point's per-shape choice
+VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, -1]  # -1: the default entry point's per-shape choice
 # (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
 # epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
 SHAPES = [
@@ -159,18 +159,18 @@ def test_repeated_calls_deterministic(vg, orc):
     assert torch.equal(first, again)
 
 
-@pytest.mark.parametrize("shape", [(256, 2048, 32768), (512, 8192, 32768)])
+@pytest.mark.parametrize("shape", [(256, 2048, 32768), (512, 8192, 32768), (2560, 4096, 32768)])
 def test_long_k_acceptance(vg, orc, shape):
     """K = 32768 (the sharded config's K) on sampled rows, against the fp64 product.
 
     fp32-output build, every version: max abs error <= 2e-2·sqrt(K/1024), and per element
     |c - r| <= that bound + 1e-2·|r| (the reference's check_error form, utils.cuh:70-118,
-    with the BASELINE tolerances). Default entry point, fp16 output: the bounded relative
-    error |c - r| / max(|r|, abs bound) is within 1e-2, or no worse than cuBLAS's fp16 GEMM
-    on the same rows. (One accumulation chain per output over K = 32768 reaches 1.3e-2 on
-    a few elements, because the tensor cores' accumulation rounds toward zero; cuBLAS keeps
-    one chain at 512×8192 and splits K at 256×2048, as stream-K does here.) v8, which adds
-    4096-long chunks into an fp32 running sum, meets max rel <= 1e-2 outright."""
+    with the BASELINE tolerances). The versions that split every output's sum (v8, v9 and
+    stream-K v4) and the default entry point, in fp32 and in fp16 output, also meet the
+    bounded relative error |c - r| / max(|r|, abs bound) <= 1e-2. (One tensor-core chain per
+    output over K = 32768 reaches 1.3e-2 on a few elements, because the tensor cores'
+    accumulation rounds toward zero; from K = 16384 on the default entry point therefore
+    only picks v9 (a full wave of 256×512 tiles: 2560×4096), v8 or v4.)"""
     import torch
     M, N, K = shape
     A, B = orc.make_inputs(M, N, K)
@@ -178,6 +178,8 @@ def test_long_k_acceptance(vg, orc, shape):
     exact = np.concatenate([orc.gemm_f64(A, B, r, 1) for r in rows])
     bound = 2e-2 * np.sqrt(K / 1024.0)
     dA, dB = to_dev(A), to_dev(B)
+    auto = vg.plan(-1, M, N, K, 256, 256, 256)["version"]
+    assert auto in (4, 8, 9), auto
     for v in VERSIONS:
         C = vg.gemm_f32out(dA, dB, version=v)
         torch.cuda.synchronize()
@@ -185,12 +187,39 @@ def test_long_k_acceptance(vg, orc, shape):
         acc = orc.acceptance(c, exact, K=K)
         assert acc["max_abs"] <= bound, (v, acc)
         assert np.all(np.abs(c - exact) <= bound + 1e-2 * np.abs(exact)), (v, acc)
-        if v == 8:  # chunked accumulation with an fp32 running sum: the strict bound holds
+        if v in (4, 8, 9, -1):  # every output's sum split: the strict bound holds
             assert acc["max_rel"] <= 1e-2, (v, acc)
-    cb16 = vg.cublas_gemm(dA, dB)
     C16 = vg.gemm(dA, dB)
     torch.cuda.synchronize()
-    acc_cb16 = orc.acceptance(cb16.cpu().numpy()[rows].astype(np.float32), exact, K=K)
     acc16 = orc.acceptance(C16.cpu().numpy()[rows].astype(np.float32), exact, K=K)
-    assert acc16["max_abs"] <= bound, (acc16, acc_cb16)
-    assert acc16["max_rel"] <= max(1e-2, 1.05 * acc_cb16["max_rel"]), (acc16, acc_cb16)
+    assert acc16["max_abs"] <= bound, acc16
+    assert acc16["max_rel"] <= 1e-2, acc16
+    assert vg.device_status() == 0
+
+
+def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
+    """The sharded config's full problem, M = N = K = 32768, through the default entry point
+    (v9: run-time tiles, chunked accumulation), on rows sampled across the whole M range
+    against the fp64 product of the oracle: max abs <= 2e-2·sqrt(K/1024) and bounded max
+    relative error <= 1e-2, fp16 output. Inputs: uniform[-1,1] fp16 from a seeded device
+    generator (the rows and B are copied to the host for the oracle)."""
+    import torch
+    M = N = K = 32768
+    assert vg.plan(-1, M, N, K, 256, 256, 256)["version"] == 9
+    g = torch.Generator(device="cuda")
+    g.manual_seed(42)
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    g.manual_seed(77)
+    dB = torch.empty((N, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    C = vg.gemm(dA, dB)
+    torch.cuda.synchronize()
+    assert vg.device_status() == 0
+    rows = [0, 1, 4097, 12345, 16384, 20000, 30001, M - 1]
+    A_rows = to_host(dA[rows])
+    B_host = to_host(dB)
+    del dA
+    exact = orc.gemm_f64(A_rows, B_host)
+    got = C[rows].cpu().numpy().astype(np.float64)
+    acc = orc.acceptance(got, exact, K=K)
+    assert acc["max_abs"] <= acc["abs_bound"], acc
+    assert acc["max_rel"] <= 1e-2, acc

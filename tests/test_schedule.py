@@ -67,7 +67,7 @@ def test_stream_k_plan(vg):
                                    (1000, 3000, 2048), (4096, 14336, 4096), (4096, 4096, 14336),
                                    (8192, 8192, 512), (32768, 32768, 32768), (4096, 32768, 32768),
                                    (256, 2048, 32768), (1000, 3000, 8192)])
-@pytest.mark.parametrize("version", [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("version", [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9])
 def test_launch_plans_cover_every_iteration_once(vg, shape, version):
     """For the plan the launcher builds (grid, raster group, stream-K or not), the workers'
     units cover every (tile, k-block) iteration of the problem exactly once."""
@@ -76,6 +76,19 @@ def test_launch_plans_cover_every_iteration_once(vg, shape, version):
     num_m, num_n, kb = p["num_m_tiles"], p["num_n_tiles"], p["num_kb"]
     if not p["persistent"]:
         assert p["grid"] == num_m * num_n * p["cta_group"]  # one CTA (pair) per tile
+        return
+    if p["dyn"]:
+        # Run-time claims: pair w starts with tile w (every pair has one: the grid is at most
+        # the tile count), later claims are workers + counter value, so the tiles claimed
+        # before the counter passes the end are each claimed once.
+        workers = p["grid"] // p["cta_group"]
+        total = num_m * num_n
+        assert 1 <= workers <= total
+        claimed = list(range(workers)) + [workers + c for c in range(total - workers)]
+        assert sorted(claimed) == list(range(total))
+        # the chunks of a tile cover its k-blocks
+        chunks = -(-kb // p["promote_kb"])
+        assert (chunks - 1) * p["promote_kb"] < kb <= chunks * p["promote_kb"]
         return
     workers = p["grid"] // p["cta_group"]
     covered = collections.Counter()

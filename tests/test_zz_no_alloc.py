@@ -3,7 +3,7 @@
 It serves callers that may not allocate device memory (a host that owns the whole GPU
 through its own pool, latency-critical loops, fixed memory budgets): the K-padding
 workspace that vg_b200_gemm_f16 takes from the stream-ordered pool comes instead from a
-fixed 32 MiB array inside the library. This file is collected last on purpose, so that a
+fixed 64 MiB array inside the library. This file is collected last on purpose, so that a
 run stopping at its first failure has already run every other test; it also passes on its
 own in a fresh process.
 """
@@ -72,7 +72,7 @@ def test_noalloc_matches_default_on_two_calls_in_a_row(vg, orc):
 def test_noalloc_rejects_padded_problems_beyond_the_limit(vg):
     import torch
     f_noalloc, _ = _c_abi(vg)
-    M, N, K = 4096, 4096, 4100  # padded copies: 8192 rows * 4104 * 2 B = 67 MB > 32 MiB
+    M, N, K = 4096, 4096, 8196  # padded copies: 8192 rows * 8200 * 2 B = 134 MB > 64 MiB
     A = torch.zeros(M, K, dtype=torch.float16, device="cuda")
     B = torch.zeros(N, K, dtype=torch.float16, device="cuda")
     C = torch.full((M, N), 3.0, dtype=torch.float16, device="cuda")

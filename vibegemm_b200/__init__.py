@@ -65,7 +65,7 @@ EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
                "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version", "stream_k",
-               "promote")
+               "promote", "dyn", "promote_kb")
 EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32", 3: "tma_f16_peers", 4: "staged_f16"}
 
 
@@ -146,7 +146,7 @@ NOALLOC_SCRATCH_LIMIT = 2001  # VG_ERROR_NOALLOC_SCRATCH_LIMIT
 
 def gemm_noalloc(A, B, out=None, stream=None):
     """vg_b200_gemm_f16 without any device allocation: the K-padding workspace is a fixed
-    32 MiB array in the library (problems whose padded copies exceed it raise
+    64 MiB array in the library (problems whose padded copies exceed it raise
     VibeGemmError with code NOALLOC_SCRATCH_LIMIT). Overlapping calls on one GPU race on
     that array; the caller must allocate `out` itself to avoid torch's allocator."""
     import torch

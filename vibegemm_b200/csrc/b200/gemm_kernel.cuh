@@ -86,7 +86,16 @@ struct GemmArgs {
     float *sk_partials;
     unsigned *sk_flags;
     int promote_kb; // PROMOTE kernels: k-blocks per accumulation chunk
+    // PROMOTE with the 256×512 pair tile: one running-sum slot of 128 × 512 fp32 per CTA
+    // (column-quad major), used only when a tile has more than one chunk.
+    float *promote_slots;
+    // DYN kernels: tile claim counter, zeroed before the launch.
+    unsigned *sched_ctr;
 };
+
+// DYN: depth of the tile-index ring through which the leader CTA's producer hands each
+// claimed tile to the other roles of the pair.
+constexpr int kSchedDepth = 4;
 
 template <int CG, int BN_> struct TileCfg {
     static_assert(BN_ == 256 || (BN_ == 192 && CG == 1) || (BN_ == 512 && CG == 2),
@@ -146,10 +155,13 @@ template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
                                          ? T::EPI_WARPS * EPI_BUFS * T::STG_BYTES
                                          : 0;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
-    static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+    // full/empty per stage, tfull/tempty per accumulator, drain, then the DYN ring's
+    // full/empty per entry.
+    static constexpr int NUM_BARS = 2 * STAGES + 4 + 1 + 2 * kSchedDepth;
     static constexpr int SLOT_OFF = BAR_OFF + 8 * NUM_BARS;
     static constexpr int ABORT_OFF = SLOT_OFF + 4;
-    static constexpr int BYTES = ABORT_OFF + 4;
+    static constexpr int RING_OFF = ABORT_OFF + 4; // int tile[kSchedDepth]
+    static constexpr int BYTES = RING_OFF + 4 * kSchedDepth;
     static constexpr int DYN_BYTES = BYTES + 1024; // slack for 1024-B alignment
     static_assert(DYN_BYTES <= kSmemLimit, "pipeline stages do not fit in shared memory");
 };
@@ -224,12 +236,24 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
 }
 
 // PROMOTE: each tile's K range is cut into chunks of args.promote_kb k-blocks; every chunk
-// is accumulated by the tensor cores from zero in TMEM buffer 0, and the epilogue warps add
-// it in fp32 (round to nearest) into a running sum kept in TMEM buffer 1. Each output then
-// sums short tensor-core chains instead of one long one (the tensor cores' accumulation
-// rounds toward zero, an error that grows with the chain). No accumulator double buffering:
-// the MMA waits while a chunk is added in. Requires ACC_BUFS == 2 and no stream-K.
-template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false>
+// is accumulated by the tensor cores from zero, and the epilogue warps add it in fp32
+// (round to nearest) into a running sum. Each output then sums short tensor-core chains
+// instead of one long one (the tensor cores' accumulation rounds toward zero, an error that
+// grows with the chain). With two TMEM buffers (BN = 256) the running sum is TMEM buffer 1
+// and the MMA waits while a chunk is added in. With the 256×512 pair tile, which fills TMEM,
+// the running sum is a per-CTA slot in global memory (args.promote_slots, L2-resident): the
+// epilogue loads each half of a finished chunk into registers, hands the half back to the
+// MMA at once and then adds it into the slot, so the next chunk's MMAs overlap the adds;
+// the last chunk adds the slot into its values on the way to the C store. No stream-K.
+//
+// DYN (CTA pairs): tiles are claimed at run time instead of by the static walk. Each pair
+// starts with tile cluster_id; afterwards the leader CTA's producer claims the next tile
+// with an atomic counter (args.sched_ctr, zeroed before the launch) and posts its index into
+// a kSchedDepth-deep ring in both CTAs' shared memory, from which the other roles of both
+// CTAs take it (full/empty mbarriers per entry; the peer's roles arrive remotely). Pairs that
+// finish early take more tiles, as with hardware-placed pairs, while the epilogue of one
+// tile still overlaps the next tile's main loop.
+template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false, bool DYN = false>
 __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
@@ -237,7 +261,9 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
     using T = TileCfg<CG, BN>;
     using L = SmemLayout<CG, BN, STAGES, EPI>;
-    static_assert(!PROMOTE || (T::ACC_BUFS == 2 && !SK), "PROMOTE needs two TMEM buffers, no stream-K");
+    static_assert(!PROMOTE || ((T::ACC_BUFS == 2 || CG == 2) && !SK),
+                  "PROMOTE: two TMEM buffers or the pair tile, no stream-K");
+    static_assert(!DYN || (CG == 2 && !SK), "DYN: CTA pairs, no stream-K");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = ptx::smem_u32(smem_raw);
@@ -261,6 +287,9 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     auto tfull_bar = [&](int a) { return sBar + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return sBar + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
+    auto sfull_bar = [&](int i) { return sBar + 8u * (2 * STAGES + 5 + i); };
+    auto sempty_bar = [&](int i) { return sBar + 8u * (2 * STAGES + 5 + kSchedDepth + i); };
+    const uint32_t ring = base + L::RING_OFF;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -272,6 +301,12 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             ptx::mbar_init(tempty_bar(a), T::EPI_WARPS * CG);
         }
         ptx::mbar_init(drain_bar, 1);
+        // DYN ring (leader's entries are released by: its MMA thread, its epilogue warps,
+        // the peer's producer and the peer's epilogue warps).
+        for (int i = 0; i < kSchedDepth; ++i) {
+            ptx::mbar_init(sfull_bar(i), 1);
+            ptx::mbar_init(sempty_bar(i), 2 + 2 * T::EPI_WARPS);
+        }
         *abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -304,6 +339,50 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     const int num_clusters = static_cast<int>(gridDim.x) / CG;
     const unsigned long long tmo = args.timeout_ns;
 
+    // ── DYN tile ring ──
+    const int total_tiles = args.num_m_tiles * args.num_n_tiles;
+    int ring_seq = 0; // entries this thread has posted or taken
+    auto dyn_fill = [&](int t, WorkUnit &u) {
+        raster_tile(t, args.num_m_tiles, args.num_n_tiles, args.group_m, u.tile_m, u.tile_n);
+        u.kb0 = 0;
+        u.kb1 = args.num_kb;
+        u.kind = kUnitFull;
+        u.first_contrib = u.last_contrib = -1;
+    };
+    // Leader producer: claim the next tile (>= total_tiles: none left) and post it to both CTAs.
+    auto ring_post = [&](int &t) -> bool {
+        const int i = ring_seq % kSchedDepth;
+        const uint32_t ph = static_cast<uint32_t>(ring_seq / kSchedDepth) & 1u;
+        t = (ring_seq == 0) ? cluster_id : num_clusters + static_cast<int>(atomicAdd(args.sched_ctr, 1u));
+        if (t > total_tiles)
+            t = total_tiles;
+        if (!wait_bar(sempty_bar(i), ph ^ 1u, abort_flag, tmo, kStatusTimeoutProducer))
+            return false;
+        ptx::st_shared_u32(ring + 4u * i, static_cast<uint32_t>(t));
+        ptx::st_shared_cluster_u32(ptx::mapa(ring + 4u * i, 1), static_cast<uint32_t>(t));
+        ptx::mbar_arrive(sfull_bar(i));
+        ptx::mbar_arrive_cluster(ptx::mapa(sfull_bar(i), 1));
+        ++ring_seq;
+        return true;
+    };
+    // Any other role (one thread): take the next entry and release it on the leader.
+    auto ring_release = [&](int i) {
+        if (rank == 0)
+            ptx::mbar_arrive(sempty_bar(i));
+        else
+            ptx::mbar_arrive_cluster(ptx::mapa(sempty_bar(i), 0));
+    };
+    auto ring_take = [&](int &t, unsigned code, unsigned backoff_ns) -> bool {
+        const int i = ring_seq % kSchedDepth;
+        const uint32_t ph = static_cast<uint32_t>(ring_seq / kSchedDepth) & 1u;
+        if (!wait_bar(sfull_bar(i), ph, abort_flag, tmo, code, backoff_ns))
+            return false;
+        t = static_cast<int>(ptx::ld_shared_u32(ring + 4u * i));
+        ring_release(i);
+        ++ring_seq;
+        return true;
+    };
+
     if (warp == 0) {
         // ───────────────────────── TMA producer ─────────────────────────
         if (lane == 0) {
@@ -315,7 +394,19 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                     args.num_kb);
             WorkUnit u;
-            while (ok && it.next(u)) {
+            auto next_unit = [&]() -> bool {
+                if constexpr (DYN) {
+                    int t = total_tiles;
+                    ok = (rank == 0) ? ring_post(t) : ring_take(t, kStatusTimeoutProducer, 0);
+                    if (!ok || t >= total_tiles)
+                        return false;
+                    dyn_fill(t, u);
+                    return true;
+                } else {
+                    return it.next(u);
+                }
+            };
+            while (ok && next_unit()) {
                 const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
                 const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
                 for (int kb = u.kb0; kb < u.kb1; ++kb) {
@@ -401,9 +492,21 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                     args.num_kb);
             WorkUnit u;
-            while (ok && it.next(u)) {
+            auto next_unit = [&]() -> bool {
+                if constexpr (DYN) {
+                    int t = total_tiles;
+                    ok = ring_take(t, kStatusTimeoutMma, 0);
+                    if (!ok || t >= total_tiles)
+                        return false;
+                    dyn_fill(t, u);
+                    return true;
+                } else {
+                    return it.next(u);
+                }
+            };
+            while (ok && next_unit()) {
                 const int nkb = u.kb1 - u.kb0; // k-blocks of this unit; MMAs index them from 0
-                if constexpr (PROMOTE) {
+                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
                     for (int c0 = 0; c0 < nkb && ok; c0 += args.promote_kb) {
                         const int c1 = min(nkb, c0 + args.promote_kb);
                         if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo,
@@ -456,55 +559,63 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                     if (acc == 0)
                         acc_phase ^= 1u;
                 } else {
-                    // Half 0 runs ahead over the first `run` k-blocks while the epilogue
-                    // still drains half 1 of the previous tile.
-                    if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    ptx::tc_fence_after();
-                    const int run = nkb < STAGES ? nkb : STAGES;
-                    const int s0 = stage;
-                    const uint32_t p0 = phase;
-                    for (int kb = 0; kb < run; ++kb) {
-                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                    // One accumulator (both halves of TMEM). PROMOTE cuts the tile's K range
+                    // into chunks, each accumulated from zero; otherwise one chunk = the tile.
+                    // Per chunk, half 0 runs ahead over the first `run` k-blocks while the
+                    // epilogue still drains half 1 of the previous chunk or tile.
+                    const int chunk = PROMOTE ? args.promote_kb : nkb;
+                    for (int c0 = 0; c0 < nkb && ok; c0 += chunk) {
+                        const int n = (nkb - c0) < chunk ? (nkb - c0) : chunk;
+                        if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
-                        issue(tmem_base, 0, kb);
-                        any = true;
-                        advance();
-                    }
-                    if (!ok)
-                        break;
-                    if (!wait_bar(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    ptx::tc_fence_after();
-                    stage = s0;
-                    phase = p0;
-                    for (int kb = 0; kb < run; ++kb) {
-                        issue(tmem_base, 1, kb);
-                        commit_to(empty_bar(stage));
-                        advance();
-                    }
-                    for (int kb = run; kb < nkb; ++kb) {
-                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                        const int run = n < STAGES ? n : STAGES;
+                        const int s0 = stage;
+                        const uint32_t p0 = phase;
+                        for (int kb = 0; kb < run; ++kb) {
+                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                            issue(tmem_base, 0, kb);
+                            any = true;
+                            advance();
+                        }
+                        if (!ok)
+                            break;
+                        if (!wait_bar(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
-                        issue(tmem_base, 0, kb);
-                        issue(tmem_base, 1, kb);
-                        commit_to(empty_bar(stage));
-                        advance();
+                        stage = s0;
+                        phase = p0;
+                        for (int kb = 0; kb < run; ++kb) {
+                            issue(tmem_base, 1, kb);
+                            commit_to(empty_bar(stage));
+                            advance();
+                        }
+                        for (int kb = run; kb < n; ++kb) {
+                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                            issue(tmem_base, 0, kb);
+                            issue(tmem_base, 1, kb);
+                            commit_to(empty_bar(stage));
+                            advance();
+                        }
+                        if (!ok)
+                            break;
+                        commit_to(tfull_bar(0));
+                        acc_phase ^= 1u;
                     }
                     if (!ok)
                         break;
-                    commit_to(tfull_bar(0));
-                    acc_phase ^= 1u;
                 }
             }
             // Every MMA issued by this thread must complete before TMEM is freed.
@@ -542,7 +653,34 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                                           (T::BM * T::BN);
         };
         bool epi_ok = true;
-        while (epi_ok && it.next(u)) {
+        auto next_unit = [&]() -> bool {
+            if constexpr (DYN) {
+                // Lane 0 takes the ring entry; the warp shares it.
+                int t = total_tiles, got = 1;
+                if (lane == 0)
+                    got = ring_take(t, kStatusTimeoutEpilogue, VG_EPI_BACKOFF_NS) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                t = __shfl_sync(0xffffffffu, t, 0);
+                if (!got) {
+                    epi_ok = false;
+                    return false;
+                }
+                if (t >= total_tiles)
+                    return false;
+                dyn_fill(t, u);
+                return true;
+            } else {
+                return it.next(u);
+            }
+        };
+        // PROMOTE with one accumulator: this CTA's running-sum slot, column-quad major
+        // ([BN/4 quads][128 rows][4 floats]: a warp's 32 rows of one quad are 512
+        // contiguous bytes).
+        float *const pslot = (PROMOTE && T::ACC_BUFS == 1 && args.promote_slots)
+                                 ? args.promote_slots + static_cast<long long>(blockIdx.x) * (T::BM * T::BN)
+                                 : nullptr;
+        const long long prow = (static_cast<long long>(sub) * 32 + lane) * 4;
+        while (epi_ok && next_unit()) {
           // PROMOTE: one pass per K chunk; only the last one stores C.
           const int nkc = PROMOTE ? (u.kb1 - u.kb0 + args.promote_kb - 1) / args.promote_kb : 1;
           for (int j = 0; j < nkc && epi_ok; ++j) {
@@ -563,8 +701,60 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             }
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
+            bool drained = false; // a non-final chunk went into the running-sum slot
+            if constexpr (PROMOTE && T::ACC_BUFS == 1) {
+                if (j + 1 < nkc) {
+                    // Per half: this warp's chunks of the half into registers, the half back
+                    // to the MMA issuer, then slot = (j == 0 ? 0 : slot) + chunk values.
+                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS; // warp's chunks per half
 #pragma unroll 1
-            for (int c = group; c < T::NCHUNK; c += T::EPI_GROUPS) {
+                    for (int h = 0; h < T::NSUB; ++h) {
+                        uint32_t v[CPH][2][32];
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
+                        }
+                        ptx::tmem_wait_ld();
+                        ptx::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+#pragma unroll
+                            for (int p = 0; p < 2; ++p) {
+                                float *dst = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
+                                if (j == 0) {
+#pragma unroll
+                                    for (int q = 0; q < 8; ++q)
+                                        *reinterpret_cast<uint4 *>(dst + q * (T::BM * 4)) =
+                                            make_uint4(v[i][p][4 * q], v[i][p][4 * q + 1], v[i][p][4 * q + 2],
+                                                       v[i][p][4 * q + 3]);
+                                } else {
+                                    float4 o[8];
+#pragma unroll
+                                    for (int q = 0; q < 8; ++q)
+                                        o[q] = *reinterpret_cast<const float4 *>(dst + q * (T::BM * 4));
+#pragma unroll
+                                    for (int q = 0; q < 8; ++q) {
+                                        o[q].x += __uint_as_float(v[i][p][4 * q]);
+                                        o[q].y += __uint_as_float(v[i][p][4 * q + 1]);
+                                        o[q].z += __uint_as_float(v[i][p][4 * q + 2]);
+                                        o[q].w += __uint_as_float(v[i][p][4 * q + 3]);
+                                        *reinterpret_cast<float4 *>(dst + q * (T::BM * 4)) = o[q];
+                                    }
+                                }
+                            }
+                        }
+                    }
+                    drained = true;
+                }
+            }
+#pragma unroll 1
+            for (int c = group; c < T::NCHUNK && !drained; c += T::EPI_GROUPS) {
                 uint32_t v0[32], v1[32];
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
@@ -583,7 +773,28 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
                     }
                 }
-                if constexpr (PROMOTE) {
+                if constexpr (PROMOTE && T::ACC_BUFS == 1) {
+                    // Last chunk of a tile with earlier chunks: add the running-sum slot.
+                    if (nkc > 1) {
+#pragma unroll
+                        for (int p = 0; p < 2; ++p) {
+                            uint32_t *v = p ? v1 : v0;
+                            const float *src = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
+                            float4 o[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                o[q] = *reinterpret_cast<const float4 *>(src + q * (T::BM * 4));
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                v[4 * q] = __float_as_uint(o[q].x + __uint_as_float(v[4 * q]));
+                                v[4 * q + 1] = __float_as_uint(o[q].y + __uint_as_float(v[4 * q + 1]));
+                                v[4 * q + 2] = __float_as_uint(o[q].z + __uint_as_float(v[4 * q + 2]));
+                                v[4 * q + 3] = __float_as_uint(o[q].w + __uint_as_float(v[4 * q + 3]));
+                            }
+                        }
+                    }
+                }
+                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
                     // Running sum of the earlier chunks: buffer 1, same lanes and columns.
                     const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                                            static_cast<uint32_t>(T::ACC_STRIDE + c * 64);

@@ -22,6 +22,12 @@
 //   v6  v3 launched with one CTA pair per tile, placed by the hardware as pairs free up
 //       (no epilogue overlap, but no static tile-to-SM assignment): for very long K,
 //       where the static schedule's slowest pairs set the end of the launch.
+//   v7  v5 with a fifth pipeline stage (long K over under-filled grids).
+//   v8  v2 with chunked accumulation: each 4096-long K chunk is summed by the tensor
+//       cores from zero and added in fp32 into a running sum in TMEM buffer 1.
+//   v9  v3's 256×512 pair tile, persistent, with tiles claimed at run time (atomic
+//       counter; pairs that finish early take more tiles) and, for K >= 16384, chunked
+//       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
 //   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
@@ -57,6 +63,7 @@ struct VersionDesc {
     int group_m;
     bool stream_k = false;
     bool promote = false; // chunked accumulation with an fp32 running sum (accurate long K)
+    bool dyn = false;     // tiles claimed at run time (atomic counter) by the persistent pairs
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -69,9 +76,27 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v6", 2, 512, 4, false, true, 16},
     {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
     {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true},
+    {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
+
+// Chunked accumulation. v8: k-blocks (of 64) per tensor-core chunk, K = 4096, which cuts
+// the rounding-toward-zero drift of one 32768-long chain to about a third. v9 promotes only
+// from K = kPromoteMinK on (below it one chain stays well inside the 1e-2 bound: the
+// bounded relative error of one chain grows about linearly with K, 1.3e-2 at K = 32768),
+// with chunks of K = 8192 up to K = 49152 and of K = 4096 beyond: each chunk boundary
+// costs the pair tile a drain of its accumulator into the running-sum slot.
+constexpr int kPromoteKb = 64;
+constexpr int kPromoteMinK = 16384;
+
+int promote_chunk_kb(int version_promote_kind, int num_kb, int Kp) {
+    if (version_promote_kind == 1) // v8
+        return kPromoteKb;
+    if (Kp < kPromoteMinK) // v9 below the threshold: the whole tile is one chunk
+        return num_kb;
+    return num_kb <= 768 ? 128 : 64;
+}
 
 // Per-shape choice among the ladder, from the measured sweep over the BASELINE shapes:
 // the 256×512 pair tile (v3) wins whenever K is not short and there is at least one
@@ -89,10 +114,12 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
-    // Very long K: hardware-placed pairs (v6) beat the static persistent walk (+5.5 % at
-    // 32768³ under the power cap, +0.6 % at 16384³; -0.5..-8 % at K <= 8192).
-    if (K >= 16384 && t3 >= pairs)
-        return 6;
+    // Very long K: the 256×512 pair tile with run-time tile claims (the balance of
+    // hardware-placed pairs, v6, with v3's epilogue overlap) and chunked fp32 accumulation,
+    // which keeps the error of each output's sum within 1e-2 of the bound at K = 32768
+    // (one tensor-core chain reaches 1.3e-2).
+    if (K >= kPromoteMinK && t3 >= pairs)
+        return 9;
     // Full waves of pair tiles: 256×512 (v3, ~6 % more work per pair-cycle than 256×256 at
     // 8192³) against 256×256 (v2), each charged for its last partial wave. Within 1.5 % v3
     // wins: it moves a quarter less data, which the estimate does not credit (8191×8193×4099:
@@ -103,8 +130,13 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
         const double e2 = (double)((t2 + pairs - 1) / pairs) * 256;
         return e3 <= 1.015 * e2 ? 3 : 2;
     }
+    // From K = kPromoteMinK on every output's sum is split (chunked accumulation, or
+    // stream-K over split tiles): one tensor-core chain per output exceeds the 1e-2 bound
+    // at K = 32768. Below a wave of 256×512 tiles that is v8 (the 256×256 pair with its
+    // running sum in TMEM; 0-10 % slower than v2) or, over a grid at most half full, v4.
+    const bool split_chains = K >= kPromoteMinK;
     if (t2 >= pairs)
-        return 2;
+        return split_chains ? 8 : 2;
     // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
     // (v1), pair 256×256 (v2), 128×192 (v5) and stream-K over pair tiles (v4), whose split
     // tiles pay a fix-up of about 28 k-blocks (partials out, owner reads them back, the
@@ -124,6 +156,8 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
                           ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
                           : 1e300;
     const double e7 = e5 * (kb >= 64 ? 0.88 : 1.04);
+    if (split_chains)
+        return e4 <= e2 * 1.1 ? 4 : 8;
     const double best = std::min({e1, e2, e4, e5, e7});
     if (e7 == best)
         return 7;
@@ -135,9 +169,6 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
 }
 
 constexpr int kMinSkIters = 4; // k-blocks per stream-K worker at least
-// Promoting versions: k-blocks (of 64) per tensor-core accumulation chunk. K = 4096 per
-// chunk cuts the rounding-toward-zero drift of one 32768-long chain to about a third.
-constexpr int kPromoteKb = 64;
 constexpr int kMaxDevices = 64;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;
 
@@ -170,6 +201,8 @@ struct Plan {
     int grid = 0;
     int persistent = 0;
     int promote = 0;
+    int dyn = 0;
+    int promote_kb = 0; // k-blocks per accumulation chunk (num_kb: one chunk)
 };
 
 inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
@@ -213,6 +246,9 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     const long long tiles = (long long)p.num_m_tiles * p.num_n_tiles;
     p.stream_k = v.stream_k ? 1 : 0;
     p.promote = v.promote ? 1 : 0;
+    p.dyn = v.dyn ? 1 : 0;
+    p.promote_kb = v.promote ? promote_chunk_kb(v.cta_group == 2 && v.bn == 512 ? 2 : 1, p.num_kb, p.Kp)
+                             : p.num_kb;
     if (v.stream_k) {
         if (peers)
             return cudaErrorInvalidValue;
@@ -427,7 +463,7 @@ cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, i
 }
 
 // ── kernel launch ────────────────────────────────────────────────────────────
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE> struct Inst {
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> struct Inst {
     static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
     static std::atomic<unsigned long long> attr_ready; // bit per device
     static int max_clusters[kMaxDevices];
@@ -435,7 +471,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE> struct Ins
     static cudaError_t prepare(int dev) {
         if ((attr_ready.load(std::memory_order_acquire) >> dev) & 1ull)
             return cudaSuccess;
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
@@ -463,7 +499,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE> struct Ins
 
     static cudaError_t launch(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                               const GemmArgs &args, int grid, cudaStream_t s) {
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid, 1, 1);
         cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
@@ -488,24 +524,24 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE> struct Ins
         return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
     }
 };
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE>
-std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK, PROMOTE>::attr_ready{0};
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE>
-int Inst<CG, BN, STAGES, EPI, SK, PROMOTE>::max_clusters[kMaxDevices] = {};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN>
+std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>::attr_ready{0};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN>
+int Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>::max_clusters[kMaxDevices] = {};
 
-template <int CG, int BN, int STAGES, bool SK = false, bool PROMOTE = false>
+template <int CG, int BN, int STAGES, bool SK = false, bool PROMOTE = false, bool DYN = false>
 cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
                          const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                          const GemmArgs *args, int grid, cudaStream_t s) {
 #define VG_EPI_CASE(E)                                                                             \
     case E: {                                                                                      \
-        cudaError_t e = Inst<CG, BN, STAGES, E, SK, PROMOTE>::prepare(dev);                        \
+        cudaError_t e = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::prepare(dev);                   \
         if (e != cudaSuccess)                                                                      \
             return e;                                                                              \
-        max_clusters = Inst<CG, BN, STAGES, E, SK, PROMOTE>::max_clusters[dev];                    \
+        max_clusters = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::max_clusters[dev];               \
         if (query_only)                                                                            \
             return cudaSuccess;                                                                    \
-        return Inst<CG, BN, STAGES, E, SK, PROMOTE>::launch(*ma, *mb, *mc, *args, grid, s);        \
+        return Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::launch(*ma, *mb, *mc, *args, grid, s);   \
     }
     if constexpr (SK) {
         switch (epi) {
@@ -544,7 +580,10 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 5)
         return dispatch_epi<1, 192, 5>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
-    if (p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v3 and v6 (grid differs)
+    if (p.dyn && p.promote && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v9
+        return dispatch_epi<2, 512, 4, false, true, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc,
+                                                          args, grid, s);
+    if (!p.dyn && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v3 and v6 (grid differs)
         return dispatch_epi<2, 512, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
@@ -553,23 +592,33 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
 
 inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
 
-// Byte layout of a call's workspace: padded A, padded B, stream-K partials, flags.
+// Byte layout of a call's workspace: padded A, padded B, stream-K partials, running-sum
+// slots of the chunked pair-tile accumulation, then the words zeroed before every launch
+// (stream-K ready flags, the run-time tile counter).
 struct WsLayout {
-    size_t a_off = 0, b_off = 0, part_off = 0, flag_off = 0, flag_bytes = 0, total = 0;
+    size_t a_off = 0, b_off = 0, part_off = 0, slot_off = 0, flag_off = 0, ctr_off = 0;
+    size_t flag_bytes = 0, total = 0;
+    bool promote_slots = false;
 };
 
 WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
     WsLayout w;
     const size_t a = p.pad_a ? round_up_256((size_t)M * p.Kp * sizeof(__half)) : 0;
     const size_t b = p.pad_b ? round_up_256((size_t)N * p.Kp * sizeof(__half)) : 0;
-    const size_t slots = p.stream_k ? (size_t)grid : 0; // one per (worker, CTA rank)
-    const size_t part = slots * 128 * (size_t)p.bn * sizeof(float);
+    const size_t sk_slots = p.stream_k ? (size_t)grid : 0; // one per (worker, CTA rank)
+    const size_t part = sk_slots * 128 * (size_t)p.bn * sizeof(float);
+    // One 128 × BN fp32 running sum per CTA when the pair tile's K range has several chunks.
+    w.promote_slots = p.promote && p.bn == 512 && p.promote_kb < p.num_kb;
+    const size_t slot = w.promote_slots ? (size_t)grid * 128 * (size_t)p.bn * sizeof(float) : 0;
+    const size_t words = sk_slots + (p.dyn ? 1 : 0);
     w.a_off = 0;
     w.b_off = a;
     w.part_off = a + b;
-    w.flag_off = a + b + part;
-    w.flag_bytes = round_up_256(slots * sizeof(unsigned));
-    w.total = (a + b + part + (slots ? w.flag_bytes : 0));
+    w.slot_off = a + b + part;
+    w.flag_off = a + b + part + slot;
+    w.ctr_off = w.flag_off + sk_slots * sizeof(unsigned);
+    w.flag_bytes = words ? round_up_256(words * sizeof(unsigned)) : 0;
+    w.total = a + b + part + slot + w.flag_bytes;
     return w;
 }
 
@@ -581,7 +630,7 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 // exits. In host code the name `noalloc_scratch` is only a host-side stand-in for the
 // symbol; its device address comes from cudaGetSymbolAddress, looked up per device with
 // that device current.
-constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20; // 64 MiB
 static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of the array on device `dev` (current). A successful lookup is kept; a
@@ -674,6 +723,8 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     void *owned = nullptr; // pool allocation to free after the launch
     float *sk_partials = nullptr;
     unsigned *sk_flags = nullptr;
+    float *promote_slots = nullptr;
+    unsigned *sched_ctr = nullptr;
     if (wl.total) {
         char *base = nullptr;
         if (src == WsSource::Pool) {
@@ -704,9 +755,13 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
         if (p.stream_k) {
             sk_partials = reinterpret_cast<float *>(base + wl.part_off);
             sk_flags = reinterpret_cast<unsigned *>(base + wl.flag_off);
-            if (e == cudaSuccess)
-                e = cudaMemsetAsync(sk_flags, 0, wl.flag_bytes, s);
         }
+        if (wl.promote_slots)
+            promote_slots = reinterpret_cast<float *>(base + wl.slot_off);
+        if (p.dyn)
+            sched_ctr = reinterpret_cast<unsigned *>(base + wl.ctr_off);
+        if (e == cudaSuccess && wl.flag_bytes)
+            e = cudaMemsetAsync(base + wl.flag_off, 0, wl.flag_bytes, s);
         if (e != cudaSuccess) {
             if (owned)
                 (void)cudaFreeAsync(owned, s);
@@ -741,7 +796,9 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     args.timeout_ns = wait_timeout_ns();
     args.sk_partials = sk_partials;
     args.sk_flags = sk_flags;
-    args.promote_kb = kPromoteKb;
+    args.promote_kb = p.promote_kb;
+    args.promote_slots = promote_slots;
+    args.sched_ctr = sched_ctr;
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
@@ -959,10 +1016,10 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
                                 mode == 2);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[16] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
+    const int vals[18] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
                           p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
                           p.grid,      p.persistent,  p.bn,          p.version, p.stream_k,
-                          p.promote};
+                          p.promote,   p.dyn,         p.promote_kb};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }
