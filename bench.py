@@ -485,12 +485,31 @@ def run_b200(args) -> None:
         flop32 = 2.0 * M32 * N32 * K32
         ms32 = max_over_ranks(run_timed(gemm32, steps32, 3, "sharded32k gemm"))
         tf32 = flop32 / (ms32 * 1e-3) / 1e12
+        # Beside it, on the same shards: cuBLAS, and v10 (the same tile and run-time tile claims
+        # with ONE accumulation chain per output, as cuBLAS; the default splits the chains at
+        # this K so that the bounded relative error stays within 1e-2).
+        C32b = torch.empty_like(C32)
+
+        def cublas32():
+            vg.cublas_gemm(A32, B32, out=C32b, stream=stream)
+
+        def v10_32():
+            vg.gemm(A32, B32, out=C32b, version=10, stream=stream)
+
+        ms_cb = max_over_ranks(run_timed(cublas32, steps32, 3, "sharded32k cublas"))
+        ms_10 = max_over_ranks(run_timed(v10_32, steps32, 3, "sharded32k v10"))
+        del C32b
         rec = {"workload": workload_name("sharded32k"), "M": M32, "N": N32, "K": K32,
                "rows_per_gpu": prow, "n_gpus": world, "scaling": "strong", "steps": steps32,
                "kernel": vg.version_name(v32) + " (via vg_b200_gemm_f16, per-shape choice)",
                "gemm_ms": ms32, "gemm_tflops": tf32, "per_gpu_tflops": tf32 / world,
                "frac_of_n_peak": tf32 / (world * pk["tflops"]),
-               "peak_per_gpu": pk["tflops"], "inputs": "uniform[-1,1] fp16, seeded device generator"}
+               "peak_per_gpu": pk["tflops"],
+               "cublas": {"gemm_ms": ms_cb, "gemm_tflops": flop32 / (ms_cb * 1e-3) / 1e12},
+               "pct_of_cublas": ms_cb / ms32,
+               "one_chain_v10": {"gemm_ms": ms_10, "gemm_tflops": flop32 / (ms_10 * 1e-3) / 1e12,
+                                 "pct_of_cublas": ms_cb / ms_10},
+               "inputs": "uniform[-1,1] fp16, seeded device generator"}
         if world > 1:
             fused = FusedAllGatherGemm(M32, N32, K32, rank, world, multicast=True)
 

@@ -1,3 +1,6 @@
+// Interface of VibeGEMM's include/backend.cuh (AnonymousSC2026/VibeGEMM, GNU General Public
+// License v3.0), kept identical so backends drop in; see NOTICE.
+//
 // GemmBackend — the plugin interface every GEMM implementation is registered behind.
 //
 // Kept interface-identical to the reference (include/backend.cuh:7-25 of VibeGEMM) so

@@ -1,3 +1,7 @@
+// Derived from VibeGEMM's include/engine.cuh (AnonymousSC2026/VibeGEMM, licensed under the
+// GNU General Public License v3.0): kept from it with the additive changes listed below, and
+// distributed under the same licence (see NOTICE).
+//
 // BenchmarkEngine — validates and times every registered backend on one shape.
 //
 // Same procedure as the reference engine (include/engine.cuh:11-143 of VibeGEMM):

@@ -1,3 +1,6 @@
+// Interface of VibeGEMM's include/registry.cuh (AnonymousSC2026/VibeGEMM, GNU General Public
+// License v3.0), kept identical so backends drop in; see NOTICE.
+//
 // KernelRegistry — static self-registration of GEMM backends.
 //
 // Same contract as the reference registry (include/registry.cuh:10-70 of VibeGEMM):

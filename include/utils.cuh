@@ -1,3 +1,7 @@
+// Derived from VibeGEMM's include/utils.cuh (AnonymousSC2026/VibeGEMM, licensed under the
+// GNU General Public License v3.0): kept from it with the additive changes listed below, and
+// distributed under the same licence (see NOTICE).
+//
 // Host helpers of the benchmark harness: error handling, input generation, the
 // element-wise correctness check, CUDA-event timing and the TFLOPS formula.
 //

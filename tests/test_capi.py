@@ -30,7 +30,7 @@ def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
                              "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
-                             "VibeGEMM B200 v9"]
+                             "VibeGEMM B200 v9", "VibeGEMM B200 v10"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -124,12 +124,14 @@ def test_plan_tails_and_alignment(vg):
 
 def test_plan_of_run_time_tiles_and_chunks(vg):
     """v9: persistent 256x512 pairs claiming tiles at run time; K >= 16384 is summed in
-    chunks of 128 k-blocks (K = 8192) up to 768 k-blocks, 64 beyond; below, one chunk."""
+    chunks of 64 k-blocks (K = 4096); below, one chunk. v10: the same without chunks."""
     p = vg.plan(9, 32768, 32768, 32768, 256, 256, 256)
-    assert (p["dyn"], p["promote"], p["promote_kb"], p["num_kb"]) == (1, 1, 128, 512)
+    assert (p["dyn"], p["promote"], p["promote_kb"], p["num_kb"]) == (1, 1, 64, 512)
     assert p["grid"] == 148 and p["persistent"] == 1 and p["tile_n"] == 512
     assert vg.plan(9, 8192, 8192, 8192, 256, 256, 256)["promote_kb"] == 128  # one chunk of 128
     assert vg.plan(9, 8192, 8192, 65536, 256, 256, 256)["promote_kb"] == 64
+    p10 = vg.plan(10, 32768, 32768, 32768, 256, 256, 256)  # run-time tiles, one chain
+    assert (p10["dyn"], p10["promote"], p10["promote_kb"]) == (1, 0, 512)
     assert vg.plan(8, 8192, 8192, 8192, 256, 256, 256)["promote_kb"] == 64
     assert vg.plan(3, 8192, 8192, 8192, 256, 256, 256)["dyn"] == 0
     # the fused all-gather's choice for a long-K shard promotes too

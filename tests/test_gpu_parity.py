@@ -17,7 +17,7 @@ from conftest import to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
-VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, -1]  # -1: the default entry point's per-shape choice
+VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, -1]  # -1: the default entry point's per-shape choice
 # (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
 # epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
 SHAPES = [
@@ -165,9 +165,10 @@ def test_long_k_acceptance(vg, orc, shape):
 
     fp32-output build, every version: max abs error <= 2e-2·sqrt(K/1024), and per element
     |c - r| <= that bound + 1e-2·|r| (the reference's check_error form, utils.cuh:70-118,
-    with the BASELINE tolerances). The versions that split every output's sum (v8, v9 and
-    stream-K v4) and the default entry point, in fp32 and in fp16 output, also meet the
-    bounded relative error |c - r| / max(|r|, abs bound) <= 1e-2. (One tensor-core chain per
+    with the BASELINE tolerances). The versions that split every output's sum into short
+    chains (v8, v9, and stream-K v4 where it is the per-shape choice: at 512×8192 its
+    split tiles keep chains of ~28000) and the default entry point, in fp32 and in fp16
+    output, also meet the bounded relative error |c - r| / max(|r|, abs bound) <= 1e-2. (One tensor-core chain per
     output over K = 32768 reaches 1.3e-2 on a few elements, because the tensor cores'
     accumulation rounds toward zero; from K = 16384 on the default entry point therefore
     only picks v9 (a full wave of 256×512 tiles: 2560×4096), v8 or v4.)"""
@@ -187,7 +188,7 @@ def test_long_k_acceptance(vg, orc, shape):
         acc = orc.acceptance(c, exact, K=K)
         assert acc["max_abs"] <= bound, (v, acc)
         assert np.all(np.abs(c - exact) <= bound + 1e-2 * np.abs(exact)), (v, acc)
-        if v in (4, 8, 9, -1):  # every output's sum split: the strict bound holds
+        if v in (8, 9, -1) or (v == 4 and auto == 4):  # sums split into short chains
             assert acc["max_rel"] <= 1e-2, (v, acc)
     C16 = vg.gemm(dA, dB)
     torch.cuda.synchronize()
@@ -200,9 +201,12 @@ def test_long_k_acceptance(vg, orc, shape):
 def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
     """The sharded config's full problem, M = N = K = 32768, through the default entry point
     (v9: run-time tiles, chunked accumulation), on rows sampled across the whole M range
-    against the fp64 product of the oracle: max abs <= 2e-2·sqrt(K/1024) and bounded max
-    relative error <= 1e-2, fp16 output. Inputs: uniform[-1,1] fp16 from a seeded device
-    generator (the rows and B are copied to the host for the oracle)."""
+    against the fp64 product of the oracle. fp32-output build: max abs <= 2e-2·sqrt(K/1024)
+    and bounded max relative error <= 1e-2. fp16 output: bounded max relative error <= 1e-2
+    and, per element, |c - r| <= 2e-2·sqrt(K/1024) + 1e-2·|r| (the fp16 rounding alone
+    exceeds the plain abs bound where |C| >= 256, since half an fp16 ulp there is 0.125).
+    Inputs: uniform[-1,1] fp16 from a seeded device generator (the sampled rows and B are
+    copied to the host for the oracle)."""
     import torch
     M = N = K = 32768
     assert vg.plan(-1, M, N, K, 256, 256, 256)["version"] == 9
@@ -211,15 +215,23 @@ def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
     dA = torch.empty((M, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
     g.manual_seed(77)
     dB = torch.empty((N, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    rows = [0, 1, 4097, 12345, 16384, 20000, 30001, M - 1]
     C = vg.gemm(dA, dB)
     torch.cuda.synchronize()
+    c16 = C[rows].cpu().numpy().astype(np.float64)
+    del C
+    C32 = vg.gemm_f32out(dA, dB)
+    torch.cuda.synchronize()
+    c32 = C32[rows].cpu().numpy().astype(np.float64)
+    del C32
     assert vg.device_status() == 0
-    rows = [0, 1, 4097, 12345, 16384, 20000, 30001, M - 1]
     A_rows = to_host(dA[rows])
     B_host = to_host(dB)
-    del dA
+    del dA, dB
     exact = orc.gemm_f64(A_rows, B_host)
-    got = C[rows].cpu().numpy().astype(np.float64)
-    acc = orc.acceptance(got, exact, K=K)
-    assert acc["max_abs"] <= acc["abs_bound"], acc
-    assert acc["max_rel"] <= 1e-2, acc
+    a32 = orc.acceptance(c32, exact, K=K)
+    assert a32["max_abs"] <= a32["abs_bound"], a32
+    assert a32["max_rel"] <= 1e-2, a32
+    a16 = orc.acceptance(c16, exact, K=K)
+    assert a16["max_rel"] <= 1e-2, a16
+    assert np.all(np.abs(c16 - exact) <= a16["abs_bound"] + 1e-2 * np.abs(exact)), a16

@@ -119,3 +119,28 @@ def test_noalloc_stream_k_partials_live_in_the_array(vg, orc):
     bound = 2e-2 * np.sqrt(K / 1024.0)
     assert np.all(np.abs(got - exact) <= bound + 1e-2 * np.abs(exact))
     assert vg.device_status() == 0
+
+
+def test_noalloc_running_sums_live_in_the_array(vg, orc):
+    """Long K over a full wave of 256x512 pair tiles: the per-shape choice is v9, whose
+    chunked accumulation keeps one fp32 running sum per CTA (256 KB each) and a tile counter;
+    here both sit in the fixed array. Two calls in a row must equal the default entry point
+    bit for bit (same chunks, same order of additions)."""
+    import torch
+    f_noalloc, f_default = _c_abi(vg)
+    M, N, K = 2560, 4096, 16384
+    p = vg.plan(-1, M, N, K, 256, 256, 256)
+    assert p["version"] == 9 and p["promote_kb"] < p["num_kb"], p
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    dB = torch.empty((N, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    s = torch.cuda.current_stream().cuda_stream
+    ref = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+    assert f_default(dA.data_ptr(), dB.data_ptr(), ref.data_ptr(), M, N, K, s) == 0
+    for _ in range(2):
+        C = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        assert f_noalloc(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K, s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(C, ref)
+    assert vg.device_status() == 0

@@ -243,8 +243,10 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
 // and the MMA waits while a chunk is added in. With the 256×512 pair tile, which fills TMEM,
 // the running sum is a per-CTA slot in global memory (args.promote_slots, L2-resident): the
 // epilogue loads each half of a finished chunk into registers, hands the half back to the
-// MMA at once and then adds it into the slot, so the next chunk's MMAs overlap the adds;
-// the last chunk adds the slot into its values on the way to the C store. No stream-K.
+// MMA at once and then stores it (first chunk) or adds it (later chunks: red.add in L2, no
+// read latency) into the slot, so the next chunk's MMAs overlap the adds; the last chunk
+// adds the slot into its values on the way to the C store. Every slot element is only ever
+// touched by one thread, so the adds happen in chunk order (deterministic). No stream-K.
 //
 // DYN (CTA pairs): tiles are claimed at run time instead of by the static walk. Each pair
 // starts with tile cluster_id; afterwards the leader CTA's producer claims the next tile
@@ -680,6 +682,10 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                                  ? args.promote_slots + static_cast<long long>(blockIdx.x) * (T::BM * T::BN)
                                  : nullptr;
         const long long prow = (static_cast<long long>(sub) * 32 + lane) * 4;
+        // The slot's lines stay in L2 ahead of the streaming A/B tiles (evict_last): with the
+        // default policy nearly every add missed L2 and went to DRAM and back (measured: 93 %
+        // of the reduction sectors missed at 8192x8192x32768, +1.8 GB read and written).
+        const uint64_t slot_pol = (PROMOTE && T::ACC_BUFS == 1) ? ptx::l2_policy_evict_last() : 0;
         while (epi_ok && next_unit()) {
           // PROMOTE: one pass per K chunk; only the last one stores C.
           const int nkc = PROMOTE ? (u.kb1 - u.kb0 + args.promote_kb - 1) / args.promote_kb : 1;
@@ -701,182 +707,10 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             }
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
-            bool drained = false; // a non-final chunk went into the running-sum slot
-            if constexpr (PROMOTE && T::ACC_BUFS == 1) {
-                if (j + 1 < nkc) {
-                    // Per half: this warp's chunks of the half into registers, the half back
-                    // to the MMA issuer, then slot = (j == 0 ? 0 : slot) + chunk values.
-                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS; // warp's chunks per half
-#pragma unroll 1
-                    for (int h = 0; h < T::NSUB; ++h) {
-                        uint32_t v[CPH][2][32];
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
-                        }
-                        ptx::tmem_wait_ld();
-                        ptx::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0)
-                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-#pragma unroll
-                            for (int p = 0; p < 2; ++p) {
-                                float *dst = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
-                                if (j == 0) {
-#pragma unroll
-                                    for (int q = 0; q < 8; ++q)
-                                        *reinterpret_cast<uint4 *>(dst + q * (T::BM * 4)) =
-                                            make_uint4(v[i][p][4 * q], v[i][p][4 * q + 1], v[i][p][4 * q + 2],
-                                                       v[i][p][4 * q + 3]);
-                                } else {
-                                    float4 o[8];
-#pragma unroll
-                                    for (int q = 0; q < 8; ++q)
-                                        o[q] = *reinterpret_cast<const float4 *>(dst + q * (T::BM * 4));
-#pragma unroll
-                                    for (int q = 0; q < 8; ++q) {
-                                        o[q].x += __uint_as_float(v[i][p][4 * q]);
-                                        o[q].y += __uint_as_float(v[i][p][4 * q + 1]);
-                                        o[q].z += __uint_as_float(v[i][p][4 * q + 2]);
-                                        o[q].w += __uint_as_float(v[i][p][4 * q + 3]);
-                                        *reinterpret_cast<float4 *>(dst + q * (T::BM * 4)) = o[q];
-                                    }
-                                }
-                            }
-                        }
-                    }
-                    drained = true;
-                }
-            }
-#pragma unroll 1
-            for (int c = group; c < T::NCHUNK && !drained; c += T::EPI_GROUPS) {
-                uint32_t v0[32], v1[32];
-                ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
-                ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
-                ptx::tmem_wait_ld();
-                // This warp's last read of a release unit (a whole buffer, or one half of the
-                // BN=512 accumulator): hand those TMEM columns back to the MMA issuer.
-                const int unit_end = (c / T::CHUNKS_PER_UNIT + 1) * T::CHUNKS_PER_UNIT;
-                if (c + T::EPI_GROUPS >= unit_end) {
-                    const int unit = (T::ACC_BUFS == 2) ? acc : (c / T::CHUNKS_PER_UNIT);
-                    ptx::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if constexpr (CG == 1)
-                            ptx::mbar_arrive(tempty_bar(unit));
-                        else
-                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
-                    }
-                }
-                if constexpr (PROMOTE && T::ACC_BUFS == 1) {
-                    // Last chunk of a tile with earlier chunks: add the running-sum slot.
-                    if (nkc > 1) {
-#pragma unroll
-                        for (int p = 0; p < 2; ++p) {
-                            uint32_t *v = p ? v1 : v0;
-                            const float *src = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
-                            float4 o[8];
-#pragma unroll
-                            for (int q = 0; q < 8; ++q)
-                                o[q] = *reinterpret_cast<const float4 *>(src + q * (T::BM * 4));
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                v[4 * q] = __float_as_uint(o[q].x + __uint_as_float(v[4 * q]));
-                                v[4 * q + 1] = __float_as_uint(o[q].y + __uint_as_float(v[4 * q + 1]));
-                                v[4 * q + 2] = __float_as_uint(o[q].z + __uint_as_float(v[4 * q + 2]));
-                                v[4 * q + 3] = __float_as_uint(o[q].w + __uint_as_float(v[4 * q + 3]));
-                            }
-                        }
-                    }
-                }
-                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
-                    // Running sum of the earlier chunks: buffer 1, same lanes and columns.
-                    const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
-                                           static_cast<uint32_t>(T::ACC_STRIDE + c * 64);
-                    if (j > 0) {
-                        uint32_t s0[32], s1[32];
-                        ptx::tmem_ld_32x32b_x32(s_row, s0);
-                        ptx::tmem_ld_32x32b_x32(s_row + 32, s1);
-                        ptx::tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            v0[i] = __float_as_uint(__uint_as_float(v0[i]) + __uint_as_float(s0[i]));
-                            v1[i] = __float_as_uint(__uint_as_float(v1[i]) + __uint_as_float(s1[i]));
-                        }
-                    }
-                    if (j + 1 < nkc) {
-                        ptx::tmem_st_32x32b_x32(s_row, v0);
-                        ptx::tmem_st_32x32b_x32(s_row + 32, v1);
-                        ptx::tmem_wait_st();
-                        continue; // not the last chunk: nothing to store yet
-                    }
-                }
+            // Stores one 64-column chunk (accumulator chunk c, 32 rows per warp) of C in the
+            // epilogue's output form.
+            auto emit = [&](int c, uint32_t (&v0)[32], uint32_t (&v1)[32]) {
                 const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
-                if constexpr (SK) {
-                    // Partial slot layout [BN/4 column quads][128 rows][4 floats]: for a
-                    // fixed quad the 32 lanes (32 consecutive rows) touch 512 contiguous
-                    // bytes, so every partial store / load is one coalesced warp access.
-                    const long long row_off = (static_cast<long long>(sub) * 32 + lane) * 4;
-                    const long long quad0 = static_cast<long long>(c) * 16; // 64 cols = 16 quads
-                    if (u.kind == kUnitPartial) {
-                        float *dst = slot_of(it.w) + row_off;
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            *reinterpret_cast<uint4 *>(dst + (quad0 + q) * (T::BM * 4)) =
-                                make_uint4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
-                            *reinterpret_cast<uint4 *>(dst + (quad0 + 8 + q) * (T::BM * 4)) =
-                                make_uint4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]);
-                        }
-                        continue;
-                    }
-                    if (u.kind == kUnitOwner && epi_ok) {
-                        // Partials of two contributors per round trip (their 32 loads are in
-                        // flight together; reading them one by one was latency-bound), added
-                        // in contributor order.
-                        auto add4 = [](uint32_t *v, const float4 &a) {
-                            v[0] = __float_as_uint(__uint_as_float(v[0]) + a.x);
-                            v[1] = __float_as_uint(__uint_as_float(v[1]) + a.y);
-                            v[2] = __float_as_uint(__uint_as_float(v[2]) + a.z);
-                            v[3] = __float_as_uint(__uint_as_float(v[3]) + a.w);
-                        };
-                        auto ld4 = [&](const float *src, long long quad) {
-                            return *reinterpret_cast<const float4 *>(src + quad * (T::BM * 4));
-                        };
-                        int w2 = u.first_contrib;
-                        for (; w2 + 1 <= u.last_contrib; w2 += 2) {
-                            const float *s0 = slot_of(w2) + row_off;
-                            const float *s1 = slot_of(w2 + 1) + row_off;
-                            float4 a0[8], b0[8], a1[8], b1[8];
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                a0[q] = ld4(s0, quad0 + q);
-                                b0[q] = ld4(s0, quad0 + 8 + q);
-                                a1[q] = ld4(s1, quad0 + q);
-                                b1[q] = ld4(s1, quad0 + 8 + q);
-                            }
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                add4(v0 + 4 * q, a0[q]);
-                                add4(v1 + 4 * q, b0[q]);
-                                add4(v0 + 4 * q, a1[q]);
-                                add4(v1 + 4 * q, b1[q]);
-                            }
-                        }
-                        if (w2 <= u.last_contrib) {
-                            const float *s0 = slot_of(w2) + row_off;
-#pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                add4(v0 + 4 * q, ld4(s0, quad0 + q));
-                                add4(v1 + 4 * q, ld4(s0, quad0 + 8 + q));
-                            }
-                        }
-                    }
-                }
                 if constexpr (EPI == kEpiStagedF16) {
                     // C rows are not 16-B aligned (N % 8 != 0 or an offset base): stage the
                     // 32 × 64 box, then write it row by row, 32 lanes covering 64 contiguous
@@ -1023,6 +857,201 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         }
                     }
                 }
+            };
+            bool drained = false; // a non-final chunk went into the running-sum slot
+            if constexpr (PROMOTE && T::ACC_BUFS == 1) {
+                if (j + 1 < nkc) {
+                    // Per half: this warp's chunks of the half into registers, the half back
+                    // to the MMA issuer, then slot = (j == 0 ? 0 : slot) + chunk values.
+                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS; // warp's chunks per half
+#pragma unroll 1
+                    for (int h = 0; h < T::NSUB; ++h) {
+                        uint32_t v[CPH][2][32];
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
+                        }
+                        ptx::tmem_wait_ld();
+                        ptx::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+#pragma unroll
+                            for (int p = 0; p < 2; ++p) {
+                                // First chunk: store; later chunks: add in L2 (red, fire and
+                                // forget: no read latency on the way to the next half).
+                                float *dst = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    const float a0 = __uint_as_float(v[i][p][4 * q]);
+                                    const float a1 = __uint_as_float(v[i][p][4 * q + 1]);
+                                    const float a2 = __uint_as_float(v[i][p][4 * q + 2]);
+                                    const float a3 = __uint_as_float(v[i][p][4 * q + 3]);
+                                    if (j == 0)
+                                        ptx::st_global_v4_hint(dst + q * (T::BM * 4), a0, a1, a2, a3, slot_pol);
+                                    else
+                                        ptx::red_add_v4_hint(dst + q * (T::BM * 4), a0, a1, a2, a3, slot_pol);
+                                }
+                            }
+                        }
+                    }
+                    drained = true;
+                } else if (nkc > 1) {
+                    // Last chunk of a multi-chunk tile: the same per-half hand-back (the slot
+                    // reads do not hold TMEM), then running sum + chunk, stored as C.
+                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS;
+#pragma unroll 1
+                    for (int h = 0; h < T::NSUB; ++h) {
+                        uint32_t v[CPH][2][32];
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
+                        }
+                        ptx::tmem_wait_ld();
+                        ptx::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
+#pragma unroll
+                        for (int i = 0; i < CPH; ++i) {
+                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+#pragma unroll
+                            for (int p = 0; p < 2; ++p) {
+                                const float *src = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    const float4 o = ptx::ld_global_cg_v4_hint(src + q * (T::BM * 4), slot_pol);
+                                    v[i][p][4 * q] = __float_as_uint(o.x + __uint_as_float(v[i][p][4 * q]));
+                                    v[i][p][4 * q + 1] = __float_as_uint(o.y + __uint_as_float(v[i][p][4 * q + 1]));
+                                    v[i][p][4 * q + 2] = __float_as_uint(o.z + __uint_as_float(v[i][p][4 * q + 2]));
+                                    v[i][p][4 * q + 3] = __float_as_uint(o.w + __uint_as_float(v[i][p][4 * q + 3]));
+                                }
+                                // The running sum of these lines is used up: drop them from L2
+                                // (no write-back; the next tile's first chunk rewrites them). Each
+                                // quad's 32 rows are 512 contiguous bytes = 4 lines, one per 8 lanes.
+                                __syncwarp();
+                                if ((lane & 7) == 0) {
+#pragma unroll
+                                    for (int q = 0; q < 8; ++q)
+                                        ptx::discard_l2_line(src + q * (T::BM * 4));
+                                }
+                            }
+                            emit(c, v[i][0], v[i][1]);
+                        }
+                    }
+                    drained = true;
+                }
+            }
+#pragma unroll 1
+            for (int c = group; c < T::NCHUNK && !drained; c += T::EPI_GROUPS) {
+                uint32_t v0[32], v1[32];
+                ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
+                ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
+                ptx::tmem_wait_ld();
+                // This warp's last read of a release unit (a whole buffer, or one half of the
+                // BN=512 accumulator): hand those TMEM columns back to the MMA issuer.
+                const int unit_end = (c / T::CHUNKS_PER_UNIT + 1) * T::CHUNKS_PER_UNIT;
+                if (c + T::EPI_GROUPS >= unit_end) {
+                    const int unit = (T::ACC_BUFS == 2) ? acc : (c / T::CHUNKS_PER_UNIT);
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (CG == 1)
+                            ptx::mbar_arrive(tempty_bar(unit));
+                        else
+                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
+                    }
+                }
+                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
+                    // Running sum of the earlier chunks: buffer 1, same lanes and columns.
+                    const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                                           static_cast<uint32_t>(T::ACC_STRIDE + c * 64);
+                    if (j > 0) {
+                        uint32_t s0[32], s1[32];
+                        ptx::tmem_ld_32x32b_x32(s_row, s0);
+                        ptx::tmem_ld_32x32b_x32(s_row + 32, s1);
+                        ptx::tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            v0[i] = __float_as_uint(__uint_as_float(v0[i]) + __uint_as_float(s0[i]));
+                            v1[i] = __float_as_uint(__uint_as_float(v1[i]) + __uint_as_float(s1[i]));
+                        }
+                    }
+                    if (j + 1 < nkc) {
+                        ptx::tmem_st_32x32b_x32(s_row, v0);
+                        ptx::tmem_st_32x32b_x32(s_row + 32, v1);
+                        ptx::tmem_wait_st();
+                        continue; // not the last chunk: nothing to store yet
+                    }
+                }
+                if constexpr (SK) {
+                    // Partial slot layout [BN/4 column quads][128 rows][4 floats]: for a
+                    // fixed quad the 32 lanes (32 consecutive rows) touch 512 contiguous
+                    // bytes, so every partial store / load is one coalesced warp access.
+                    const long long row_off = (static_cast<long long>(sub) * 32 + lane) * 4;
+                    const long long quad0 = static_cast<long long>(c) * 16; // 64 cols = 16 quads
+                    if (u.kind == kUnitPartial) {
+                        float *dst = slot_of(it.w) + row_off;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            *reinterpret_cast<uint4 *>(dst + (quad0 + q) * (T::BM * 4)) =
+                                make_uint4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]);
+                            *reinterpret_cast<uint4 *>(dst + (quad0 + 8 + q) * (T::BM * 4)) =
+                                make_uint4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]);
+                        }
+                        continue;
+                    }
+                    if (u.kind == kUnitOwner && epi_ok) {
+                        // Partials of two contributors per round trip (their 32 loads are in
+                        // flight together; reading them one by one was latency-bound), added
+                        // in contributor order.
+                        auto add4 = [](uint32_t *v, const float4 &a) {
+                            v[0] = __float_as_uint(__uint_as_float(v[0]) + a.x);
+                            v[1] = __float_as_uint(__uint_as_float(v[1]) + a.y);
+                            v[2] = __float_as_uint(__uint_as_float(v[2]) + a.z);
+                            v[3] = __float_as_uint(__uint_as_float(v[3]) + a.w);
+                        };
+                        auto ld4 = [&](const float *src, long long quad) {
+                            return *reinterpret_cast<const float4 *>(src + quad * (T::BM * 4));
+                        };
+                        int w2 = u.first_contrib;
+                        for (; w2 + 1 <= u.last_contrib; w2 += 2) {
+                            const float *s0 = slot_of(w2) + row_off;
+                            const float *s1 = slot_of(w2 + 1) + row_off;
+                            float4 a0[8], b0[8], a1[8], b1[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                a0[q] = ld4(s0, quad0 + q);
+                                b0[q] = ld4(s0, quad0 + 8 + q);
+                                a1[q] = ld4(s1, quad0 + q);
+                                b1[q] = ld4(s1, quad0 + 8 + q);
+                            }
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                add4(v0 + 4 * q, a0[q]);
+                                add4(v1 + 4 * q, b0[q]);
+                                add4(v0 + 4 * q, a1[q]);
+                                add4(v1 + 4 * q, b1[q]);
+                            }
+                        }
+                        if (w2 <= u.last_contrib) {
+                            const float *s0 = slot_of(w2) + row_off;
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                add4(v0 + 4 * q, ld4(s0, quad0 + q));
+                                add4(v1 + 4 * q, ld4(s0, quad0 + 8 + q));
+                            }
+                        }
+                    }
+                }
+                emit(c, v0, v1);
             }
             if (SK && u.kind == kUnitPartial) {
                 // All epilogue warps' partial stores, then one release of the ready flag.

@@ -28,6 +28,8 @@
 //   v9  v3's 256×512 pair tile, persistent, with tiles claimed at run time (atomic
 //       counter; pairs that finish early take more tiles) and, for K >= 16384, chunked
 //       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
+//   v10 v9 without the chunking: one accumulation chain per output, as cuBLAS (the
+//       fastest long-K kernel; bit-identical to v3/v6).
 //   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
@@ -77,16 +79,18 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
     {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true},
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
+    {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
 
-// Chunked accumulation. v8: k-blocks (of 64) per tensor-core chunk, K = 4096, which cuts
-// the rounding-toward-zero drift of one 32768-long chain to about a third. v9 promotes only
-// from K = kPromoteMinK on (below it one chain stays well inside the 1e-2 bound: the
-// bounded relative error of one chain grows about linearly with K, 1.3e-2 at K = 32768),
-// with chunks of K = 8192 up to K = 49152 and of K = 4096 beyond: each chunk boundary
-// costs the pair tile a drain of its accumulator into the running-sum slot.
+// Chunked accumulation: k-blocks (of 64) per tensor-core chunk, K = 4096. The tensor cores'
+// fp32 accumulation rounds toward zero, and the error of one chain grows about linearly with
+// its length: the bounded relative error |c - r| / max(|r|, 2e-2·sqrt(K/1024)) of one chain,
+// on uniform[-1,1] inputs (16 sampled rows of M = N = K), is 0.82e-2 at K = 8192, 2.0e-2 at
+// 16384 and 3.6e-2 at 32768 (cuBLAS's identical), and with chunks of 4096 it is 0.41e-2 at
+// K = 32768 (8192-long chunks: 1.03e-2). v8 always chunks; v9 chunks from K = kPromoteMinK
+// on (below it one chunk: the whole tile).
 constexpr int kPromoteKb = 64;
 constexpr int kPromoteMinK = 16384;
 
@@ -95,7 +99,7 @@ int promote_chunk_kb(int version_promote_kind, int num_kb, int Kp) {
         return kPromoteKb;
     if (Kp < kPromoteMinK) // v9 below the threshold: the whole tile is one chunk
         return num_kb;
-    return num_kb <= 768 ? 128 : 64;
+    return kPromoteKb;
 }
 
 // Per-shape choice among the ladder, from the measured sweep over the BASELINE shapes:
@@ -583,6 +587,9 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
     if (p.dyn && p.promote && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v9
         return dispatch_epi<2, 512, 4, false, true, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc,
                                                           args, grid, s);
+    if (p.dyn && !p.promote && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v10
+        return dispatch_epi<2, 512, 4, false, false, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc,
+                                                           args, grid, s);
     if (!p.dyn && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v3 and v6 (grid differs)
         return dispatch_epi<2, 512, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
