@@ -48,16 +48,16 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
  * allocation could stall or fail under memory pressure, and hosts with a device-memory
  * budget fixed at start-up. vg_b200_gemm_f16 takes the buffer for its K-padding pre-pass
  * (needed when K % 8 != 0 or A/B is not 16-byte aligned) from the CUDA stream-ordered
- * pool; this entry point uses a fixed 64 MiB array in the library's device memory
+ * pool; this entry point uses a fixed 32 MiB array in the library's device memory
  * instead and never calls cudaMalloc, cudaMallocAsync, cudaFree or an allocating library.
- *   - Limit: the call's workspace must fit in 64 MiB: a padded copy of each operand that
+ *   - Limit: the call's workspace must fit in 32 MiB: a padded copy of each operand that
  *     needs one (M * roundup(K, 8) * 2 bytes for A, N * roundup(K, 8) * 2 bytes for B), plus
  *     for small grids that use stream-K scheduling the fp32 partial tiles and their flags
- *     (at most 148 * 128 KB = 18.5 MiB), plus for K >= 16384 on the 256x512 pair tile the
- *     fp32 running sums of the chunked accumulation (148 * 256 KB = 37 MiB). Larger
- *     workspaces return VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing. Problems that
- *     need none of these have no size limit.
- *   - The 64 MiB belong to the library's device code. With CUDA's lazy module loading
+ *     (at most 148 * 128 KB = 18.5 MiB), plus 256 bytes for the tile counter of the
+ *     versions that claim tiles at run time. Larger workspaces return
+ *     VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing. Problems that need none of these
+ *     have no size limit.
+ *   - The 32 MiB belong to the library's device code. With CUDA's lazy module loading
  *     (the default) a GPU reserves them when that code is first loaded on it, i.e. at the
  *     first GEMM call of any entry point on that device, and holds them until the process
  *     exits. A host that gives all of a GPU's memory to its own pool must make one call on
@@ -67,9 +67,8 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
  *     lookup is returned as that call's error and retried by the next call.
  *   - All calls share the array: calls that overlap on the GPU (different streams, or
  *     different host threads on one device) race on it; serialise them. Each call
- *     rewrites every scratch byte it reads (a running sum's first chunk is stored, not
- *     added) and zeroes its stream-K flags and tile counter itself (cudaMemsetAsync), so
- *     nothing needs clearing between calls.
+ *     rewrites every scratch byte it reads and zeroes its stream-K flags and tile counter
+ *     itself (cudaMemsetAsync), so nothing needs clearing between calls.
  * Same semantics, arguments and return codes as vg_b200_gemm_f16 otherwise. */
 #define VG_ERROR_NOALLOC_SCRATCH_LIMIT 2001
 int vg_b200_gemm_f16_noalloc(const void *A, const void *B, void *C, int M, int N, int K,

@@ -84,8 +84,8 @@ def _worker(rank, world, port, M, N, K, multicast, side_stream, q):
 @pytest.mark.parametrize("multicast", [False, True], ids=["p2p", "nvls"])
 @pytest.mark.parametrize("M,N,K", [(1536, 2048, 1024), (1001, 1024, 4099), (5120, 4096, 16384)])
 def test_fused_gemm_allgather_two_gpus(M, N, K, multicast, side_stream):
-    """(5120, 4096, 16384): each rank's 2560-row shard is a full wave of 256×512 tiles at long
-    K, so the shards run v9 (run-time tiles, chunked accumulation) with the peer epilogue."""
+    """(5120, 4096, 16384): each rank's 2560-row shard is a full wave of pair tiles at long K,
+    so the shards run v8 (run-time tiles, chunked accumulation) with the peer epilogue."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:

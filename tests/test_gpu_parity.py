@@ -171,7 +171,7 @@ def test_long_k_acceptance(vg, orc, shape):
     output, also meet the bounded relative error |c - r| / max(|r|, abs bound) <= 1e-2. (One tensor-core chain per
     output over K = 32768 reaches 1.3e-2 on a few elements, because the tensor cores'
     accumulation rounds toward zero; from K = 16384 on the default entry point therefore
-    only picks v9 (a full wave of 256×512 tiles: 2560×4096), v8 or v4.)"""
+    only picks v8 or v4.)"""
     import torch
     M, N, K = shape
     A, B = orc.make_inputs(M, N, K)
@@ -200,7 +200,7 @@ def test_long_k_acceptance(vg, orc, shape):
 
 def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
     """The sharded config's full problem, M = N = K = 32768, through the default entry point
-    (v9: run-time tiles, chunked accumulation), on rows sampled across the whole M range
+    (v8: run-time tiles, chunks of 4096 summed in TMEM), on rows sampled across the whole M range
     against the fp64 product of the oracle. fp32-output build: max abs <= 2e-2·sqrt(K/1024)
     and bounded max relative error <= 1e-2. fp16 output: bounded max relative error <= 1e-2
     and, per element, |c - r| <= 2e-2·sqrt(K/1024) + 1e-2·|r| (the fp16 rounding alone
@@ -209,7 +209,7 @@ def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
     copied to the host for the oracle)."""
     import torch
     M = N = K = 32768
-    assert vg.plan(-1, M, N, K, 256, 256, 256)["version"] == 9
+    assert vg.plan(-1, M, N, K, 256, 256, 256)["version"] == 8
     g = torch.Generator(device="cuda")
     g.manual_seed(42)
     dA = torch.empty((M, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)

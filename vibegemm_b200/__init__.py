@@ -146,7 +146,7 @@ NOALLOC_SCRATCH_LIMIT = 2001  # VG_ERROR_NOALLOC_SCRATCH_LIMIT
 
 def gemm_noalloc(A, B, out=None, stream=None):
     """vg_b200_gemm_f16 without any device allocation: the K-padding workspace is a fixed
-    64 MiB array in the library (problems whose padded copies exceed it raise
+    32 MiB array in the library (problems whose padded copies exceed it raise
     VibeGemmError with code NOALLOC_SCRATCH_LIMIT). Overlapping calls on one GPU race on
     that array; the caller must allocate `out` itself to avoid torch's allocator."""
     import torch

@@ -858,7 +858,53 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                     }
                 }
             };
-            bool drained = false; // a non-final chunk went into the running-sum slot
+            bool drained = false; // this chunk was handled by a PROMOTE path below
+            if constexpr (PROMOTE && T::ACC_BUFS == 2) {
+                // The warp's chunks of buffer 0 into registers, buffer 0 back to the MMA issuer
+                // at once (the next chunk's MMAs overlap the rest), then the running sum in
+                // TMEM buffer 1: sum = chunk (first), sum += chunk, or C = sum + chunk (last).
+                constexpr int CPW = T::NCHUNK / T::EPI_GROUPS;
+                uint32_t v[CPW][2][32];
+#pragma unroll
+                for (int i = 0; i < CPW; ++i) {
+                    const int c = group + i * T::EPI_GROUPS;
+                    ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
+                    ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
+                }
+                ptx::tmem_wait_ld();
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (CG == 1)
+                        ptx::mbar_arrive(tempty_bar(0));
+                    else
+                        ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(0), 0));
+                }
+#pragma unroll
+                for (int i = 0; i < CPW; ++i) {
+                    const int c = group + i * T::EPI_GROUPS;
+                    const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                                           static_cast<uint32_t>(T::ACC_STRIDE + c * 64);
+#pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        if (j > 0) {
+                            uint32_t sv[32];
+                            ptx::tmem_ld_32x32b_x32(s_row + 32 * p, sv);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                v[i][p][e] = __float_as_uint(__uint_as_float(v[i][p][e]) + __uint_as_float(sv[e]));
+                        }
+                        if (j + 1 < nkc)
+                            ptx::tmem_st_32x32b_x32(s_row + 32 * p, v[i][p]);
+                    }
+                    if (j + 1 < nkc)
+                        ptx::tmem_wait_st();
+                    else
+                        emit(c, v[i][0], v[i][1]);
+                }
+                drained = true;
+            }
             if constexpr (PROMOTE && T::ACC_BUFS == 1) {
                 if (j + 1 < nkc) {
                     // Per half: this warp's chunks of the half into registers, the half back
@@ -967,28 +1013,6 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                             ptx::mbar_arrive(tempty_bar(unit));
                         else
                             ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(unit), 0));
-                    }
-                }
-                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
-                    // Running sum of the earlier chunks: buffer 1, same lanes and columns.
-                    const uint32_t s_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
-                                           static_cast<uint32_t>(T::ACC_STRIDE + c * 64);
-                    if (j > 0) {
-                        uint32_t s0[32], s1[32];
-                        ptx::tmem_ld_32x32b_x32(s_row, s0);
-                        ptx::tmem_ld_32x32b_x32(s_row + 32, s1);
-                        ptx::tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            v0[i] = __float_as_uint(__uint_as_float(v0[i]) + __uint_as_float(s0[i]));
-                            v1[i] = __float_as_uint(__uint_as_float(v1[i]) + __uint_as_float(s1[i]));
-                        }
-                    }
-                    if (j + 1 < nkc) {
-                        ptx::tmem_st_32x32b_x32(s_row, v0);
-                        ptx::tmem_st_32x32b_x32(s_row + 32, v1);
-                        ptx::tmem_wait_st();
-                        continue; // not the last chunk: nothing to store yet
                     }
                 }
                 if constexpr (SK) {

@@ -23,8 +23,9 @@
 //       (no epilogue overlap, but no static tile-to-SM assignment): for very long K,
 //       where the static schedule's slowest pairs set the end of the launch.
 //   v7  v5 with a fifth pipeline stage (long K over under-filled grids).
-//   v8  v2 with chunked accumulation: each 4096-long K chunk is summed by the tensor
-//       cores from zero and added in fp32 into a running sum in TMEM buffer 1.
+//   v8  v2's 256×256 pair tile with chunked accumulation: each 4096-long K chunk is summed
+//       by the tensor cores from zero and added in fp32 into a running sum in TMEM buffer 1;
+//       tiles claimed at run time as in v9.
 //   v9  v3's 256×512 pair tile, persistent, with tiles claimed at run time (atomic
 //       counter; pairs that finish early take more tiles) and, for K >= 16384, chunked
 //       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
@@ -77,7 +78,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v5", 1, 192, 4, true, true, 8},
     {"VibeGEMM B200 v6", 2, 512, 4, false, true, 16},
     {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
-    {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true},
+    {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true, true},
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
 };
@@ -118,12 +119,15 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
-    // Very long K: the 256×512 pair tile with run-time tile claims (the balance of
-    // hardware-placed pairs, v6, with v3's epilogue overlap) and chunked fp32 accumulation,
-    // which keeps the error of each output's sum within 1e-2 of the bound at K = 32768
-    // (one tensor-core chain reaches 1.3e-2).
-    if (K >= kPromoteMinK && t3 >= pairs)
-        return 9;
+    // From K = kPromoteMinK on every output's sum is split into chains of at most 4096 (one
+    // tensor-core chain per output exceeds the 1e-2 bound from K ~ 10000 on, 3.6e-2 at
+    // 32768): v8, the 256×256 pair with its running sum in TMEM and run-time tile claims
+    // (sustained at 32768³: 1146 TFLOP/s, against 1078 for v9, whose 256×512 tile keeps the
+    // sums in global memory, and 1298 for one chain, v10), or, over a grid at most half
+    // full, stream-K v4.
+    const bool split_chains = K >= kPromoteMinK;
+    if (split_chains && t2 >= pairs)
+        return 8;
     // Full waves of pair tiles: 256×512 (v3, ~6 % more work per pair-cycle than 256×256 at
     // 8192³) against 256×256 (v2), each charged for its last partial wave. Within 1.5 % v3
     // wins: it moves a quarter less data, which the estimate does not credit (8191×8193×4099:
@@ -134,13 +138,8 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
         const double e2 = (double)((t2 + pairs - 1) / pairs) * 256;
         return e3 <= 1.015 * e2 ? 3 : 2;
     }
-    // From K = kPromoteMinK on every output's sum is split (chunked accumulation, or
-    // stream-K over split tiles): one tensor-core chain per output exceeds the 1e-2 bound
-    // at K = 32768. Below a wave of 256×512 tiles that is v8 (the 256×256 pair with its
-    // running sum in TMEM; 0-10 % slower than v2) or, over a grid at most half full, v4.
-    const bool split_chains = K >= kPromoteMinK;
     if (t2 >= pairs)
-        return split_chains ? 8 : 2;
+        return 2;
     // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
     // (v1), pair 256×256 (v2), 128×192 (v5) and stream-K over pair tiles (v4), whose split
     // tiles pay a fix-up of about 28 k-blocks (partials out, owner reads them back, the
@@ -577,9 +576,9 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 4)
         return dispatch_epi<1, 192, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
-    if (p.promote && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
-        return dispatch_epi<2, 256, 6, false, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args,
-                                                    grid, s);
+    if (p.promote && p.cta_group == 2 && p.bn == 256 && p.stages == 6) // v8
+        return dispatch_epi<2, 256, 6, false, true, true>(p.epi, dev, max_clusters, query_only, ma, mb, mc,
+                                                          args, grid, s);
     if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 5)
@@ -637,7 +636,7 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 // exits. In host code the name `noalloc_scratch` is only a host-side stand-in for the
 // symbol; its device address comes from cudaGetSymbolAddress, looked up per device with
 // that device current.
-constexpr size_t kNoAllocScratchBytes = size_t(64) << 20; // 64 MiB
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20; // 32 MiB
 static __device__ __align__(256) unsigned char noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of the array on device `dev` (current). A successful lookup is kept; a
