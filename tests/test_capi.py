@@ -30,7 +30,7 @@ def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
                              "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
-                             "VibeGEMM B200 v9", "VibeGEMM B200 v10"]
+                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]

@@ -61,6 +61,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v10 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<10>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v10
+namespace gemm_b200_v11 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<11>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v11
 // The default entry point: one of the versions above, chosen per shape.
 namespace gemm_b200_auto {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
@@ -100,4 +103,5 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v7", GeneratedB200KernelBackend<gemm_b200_v7
 REGISTER_B200_KERNEL("VibeGEMM B200 v8", GeneratedB200KernelBackend<gemm_b200_v8::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v9", GeneratedB200KernelBackend<gemm_b200_v9::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v10", GeneratedB200KernelBackend<gemm_b200_v10::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v11", GeneratedB200KernelBackend<gemm_b200_v11::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
