@@ -42,7 +42,7 @@ _SIGS = {
     "vg_shard_rows": (None, [ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
                              ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong)]),
     "vg_raster_tile": (None, [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2),
-    "vg_work_units": (ctypes.c_int, [ctypes.c_int] * 7 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "vg_work_units": (ctypes.c_int, [ctypes.c_int] * 8 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "vg_b200_plan": (ctypes.c_int, [ctypes.c_int] * 4 + [ctypes.c_size_t] * 3 + [ctypes.c_int] * 2
                      + [ctypes.POINTER(ctypes.c_int)]),
     "vg_b200_gemm_f16_allgather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
@@ -65,8 +65,9 @@ EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
                "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version", "stream_k",
-               "promote", "dyn", "promote_kb")
-EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32", 3: "tma_f16_peers", 4: "staged_f16"}
+               "promote", "dyn", "promote_kb", "splits")
+EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32", 3: "tma_f16_peers", 4: "staged_f16",
+             5: "splitk_f16"}
 
 
 class VibeGemmError(RuntimeError):
@@ -340,18 +341,18 @@ UNIT_KINDS = {0: "full", 1: "partial", 2: "owner"}
 
 
 def work_units(stream_k: bool, worker: int, workers: int, num_m: int, num_n: int, group_m: int,
-               num_kb: int) -> list[dict]:
+               num_kb: int, splits: int = 1) -> list[dict]:
     """The units a persistent worker processes (host copy of the device schedule)."""
     L = lib()
-    n = L.vg_work_units(int(stream_k), worker, workers, num_m, num_n, group_m, num_kb, None, 0)
+    n = L.vg_work_units(int(stream_k), worker, workers, num_m, num_n, group_m, num_kb, splits, None, 0)
     if n < 0:
         raise ValueError("bad schedule arguments")
-    buf = (ctypes.c_int * (7 * max(n, 1)))()
-    L.vg_work_units(int(stream_k), worker, workers, num_m, num_n, group_m, num_kb, buf, n)
-    keys = ("tile_m", "tile_n", "kb0", "kb1", "kind", "first_contrib", "last_contrib")
+    buf = (ctypes.c_int * (8 * max(n, 1)))()
+    L.vg_work_units(int(stream_k), worker, workers, num_m, num_n, group_m, num_kb, splits, buf, n)
+    keys = ("tile_m", "tile_n", "kb0", "kb1", "kind", "first_contrib", "last_contrib", "split")
     out = []
     for i in range(n):
-        d = dict(zip(keys, buf[7 * i: 7 * i + 7]))
+        d = dict(zip(keys, buf[8 * i: 8 * i + 8]))
         d["kind"] = UNIT_KINDS[d["kind"]]
         out.append(d)
     return out

@@ -50,6 +50,9 @@ enum EpiKind : int {
     kEpiDirectF32 = 2, // fp32 output, validation build of the same main loop
     kEpiTmaF16Peers = 3, // TMA store to local C + the same rows into every peer GPU's C
     kEpiStagedF16 = 4,   // smem staging + row-cooperative coalesced stores (any C alignment)
+    // Split-K with fp16 C: the kernel runs kEpiDirectF32 into an fp32 workspace and a
+    // reduction kernel writes C (a launch-plan value; no kernel is built for it).
+    kEpiSplitF16 = 5,
 };
 
 constexpr int kMaxPeers = 7; // peers of one node (8 GPUs per NVSwitch domain)
@@ -91,6 +94,10 @@ struct GemmArgs {
     float *promote_slots;
     // DYN kernels: tile claim counter, zeroed before the launch.
     unsigned *sched_ctr;
+    // Split-K (fp32 output only): the K range is cut into `splits` parts; the partial of split
+    // s is written at C + s * split_stride elements. 1 = no split.
+    int splits;
+    long long split_stride;
 };
 
 // DYN: depth of the tile-index ring through which the leader CTA's producer hands each
@@ -350,6 +357,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         u.kb1 = args.num_kb;
         u.kind = kUnitFull;
         u.first_contrib = u.last_contrib = -1;
+        u.split = 0;
     };
     // Leader producer: claim the next tile (>= total_tiles: none left) and post it to both CTAs.
     auto ring_post = [&](int &t) -> bool {
@@ -394,7 +402,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             bool ok = true;
             UnitIter it;
             it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
-                    args.num_kb);
+                    args.num_kb, args.splits);
             WorkUnit u;
             auto next_unit = [&]() -> bool {
                 if constexpr (DYN) {
@@ -492,7 +500,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             };
             UnitIter it;
             it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
-                    args.num_kb);
+                    args.num_kb, args.splits);
             WorkUnit u;
             auto next_unit = [&]() -> bool {
                 if constexpr (DYN) {
@@ -647,7 +655,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         int buf = 0;
         UnitIter it;
         it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
-                args.num_kb);
+                args.num_kb, args.splits);
         WorkUnit u;
         // Stream-K partial slot of (worker, CTA rank): 128 × BN floats.
         auto slot_of = [&](int worker) {
@@ -836,7 +844,8 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 } else {
                     const int row = row0 + lane;
                     if (row < args.M) {
-                        float *crow = static_cast<float *>(args.C) + static_cast<long long>(row) * args.ldc;
+                        float *crow = static_cast<float *>(args.C) + u.split * args.split_stride +
+                                      static_cast<long long>(row) * args.ldc;
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));

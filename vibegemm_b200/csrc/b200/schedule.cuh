@@ -37,6 +37,9 @@ VG_HD void raster_tile(int t, int num_m, int num_n, int group_m, int &tile_m, in
 // ── work units of the persistent workers ──────────────────────────────────────
 // A unit is tile (tile_m, tile_n) restricted to k-blocks [kb0, kb1).
 //   data-parallel: worker w takes whole tiles w, w+P, w+2P, ... (grouped raster).
+//   split-K:       the same walk over T·S units, T tiles times S splits of the K range:
+//                  unit u is tile u % T (raster) over k-blocks [s·KB/S, (s+1)·KB/S) with
+//                  s = u / T, whose fp32 partial goes to split s of a workspace.
 //   stream-K:      the T·KB (tile, k-block) iterations are cut into P equal contiguous
 //                  ranges, [w·W/P, (w+1)·W/P) with W = T·KB, walked in order. A unit that
 //                  starts inside a tile (kb0 > 0) is PARTIAL: its fp32 accumulator goes to
@@ -50,15 +53,17 @@ enum UnitKind : int { kUnitFull = 0, kUnitPartial = 1, kUnitOwner = 2 };
 struct WorkUnit {
     int tile_m, tile_n, kb0, kb1, kind;
     int first_contrib, last_contrib; // owner units: workers holding the other k-blocks
+    int split;                       // split-K: which K split (0 otherwise)
 };
 
 struct UnitIter {
     bool sk;
-    int w, P, num_m, num_n, group_m, KB;
+    int w, P, num_m, num_n, group_m, KB, S;
     long long i, end, W; // stream-K position
     int t;               // data-parallel position
 
-    VG_HD void init(bool stream_k, int worker, int workers, int nm, int nn, int gm, int kb) {
+    VG_HD void init(bool stream_k, int worker, int workers, int nm, int nn, int gm, int kb,
+                    int splits = 1) {
         sk = stream_k;
         w = worker;
         P = workers;
@@ -66,6 +71,7 @@ struct UnitIter {
         num_n = nn;
         group_m = gm;
         KB = kb;
+        S = splits < 1 ? 1 : splits;
         W = (long long)nm * nn * kb;
         i = begin_of(w);
         end = begin_of(w + 1);
@@ -77,13 +83,16 @@ struct UnitIter {
 
     VG_HD bool next(WorkUnit &u) {
         if (!sk) {
-            if (t >= num_m * num_n)
+            const int T = num_m * num_n;
+            if (t >= T * S)
                 return false;
-            raster_tile(t, num_m, num_n, group_m, u.tile_m, u.tile_n);
-            u.kb0 = 0;
-            u.kb1 = KB;
+            const int s = t / T;
+            raster_tile(t - s * T, num_m, num_n, group_m, u.tile_m, u.tile_n);
+            u.kb0 = (int)((long long)s * KB / S);
+            u.kb1 = (int)((long long)(s + 1) * KB / S);
             u.kind = kUnitFull;
             u.first_contrib = u.last_contrib = -1;
+            u.split = s;
             t += P;
             return true;
         }
@@ -96,6 +105,7 @@ struct UnitIter {
         raster_tile(tile, num_m, num_n, group_m, u.tile_m, u.tile_n);
         u.kb0 = k0;
         u.kb1 = k1;
+        u.split = 0;
         u.first_contrib = u.last_contrib = -1;
         if (k0 == 0 && k1 == KB) {
             u.kind = kUnitFull;

@@ -33,6 +33,9 @@
 //       fastest long-K kernel; bit-identical to v3/v6).
 //   v11 CTA pair with a 256×192 tile (each CTA loads 96 rows of B), 6-stage ring: for
 //       grids that fill one wave, 30 % fewer L2→SMEM bytes per FLOP than 128×192 (v5).
+//   v12 split-K over v2's pair tile for grids with few tiles and long K: tile × K-split
+//       units fill the pairs, each writes an fp32 partial, and a reduction kernel adds the
+//       splits in order and stores C (deterministic; every output's chain is K / splits).
 //   auto (the default entry point) picks one of them per shape (select_version).
 //
 // Shapes are unrestricted (M, N, K >= 0). TMA needs 16-B aligned bases and row
@@ -69,6 +72,7 @@ struct VersionDesc {
     bool stream_k = false;
     bool promote = false; // chunked accumulation with an fp32 running sum (accurate long K)
     bool dyn = false;     // tiles claimed at run time (atomic counter) by the persistent pairs
+    bool split_k = false; // K range split over several units, fp32 partials + reduction kernel
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -84,6 +88,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 192, 6, true, true, 8},
+    {"VibeGEMM B200 v12", 2, 256, 6, true, true, 8, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -209,6 +214,7 @@ struct Plan {
     int promote = 0;
     int dyn = 0;
     int promote_kb = 0; // k-blocks per accumulation chunk (num_kb: one chunk)
+    int splits = 1;     // split-K parts (1: none)
 };
 
 inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
@@ -255,6 +261,20 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.dyn = v.dyn ? 1 : 0;
     p.promote_kb = v.promote ? promote_chunk_kb(v.cta_group == 2 && v.bn == 512 ? 2 : 1, p.num_kb, p.Kp)
                              : p.num_kb;
+    if (v.split_k) {
+        // Enough K splits to give every pair slot a unit (one wave), at least 8 k-blocks per
+        // split, and from K = kPromoteMinK on chains of at most kPromoteKb k-blocks.
+        const int slots = std::max(1, max_clusters);
+        long long S = std::max(1LL, slots / std::max(1LL, tiles));
+        S = std::min<long long>(S, std::max(1, p.num_kb / 8));
+        if (p.Kp >= kPromoteMinK)
+            S = std::max<long long>(S, ceil_div_i(p.num_kb, kPromoteKb));
+        p.splits = (int)std::max(1LL, std::min<long long>(S, p.num_kb));
+        if (p.splits > 1 && peers)
+            return cudaErrorInvalidValue; // the all-gather epilogue has no split-K form
+        if (p.splits > 1)
+            p.epi = f32_out ? kEpiDirectF32 : kEpiSplitF16; // the reduction kernel's output
+    }
     if (v.stream_k) {
         if (peers)
             return cudaErrorInvalidValue;
@@ -264,7 +284,7 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
         p.grid = (int)workers * v.cta_group;
     } else if (v.persistent) {
         const int slots = (v.cta_group == 2) ? std::max(1, max_clusters) : num_sms;
-        p.grid = (int)std::min<long long>(tiles, slots) * v.cta_group;
+        p.grid = (int)std::min<long long>(tiles * p.splits, slots) * v.cta_group;
     } else {
         p.grid = (int)tiles * v.cta_group;
     }
@@ -468,6 +488,63 @@ cudaError_t launch_pad(const void *src, long long rows, int cols, __half *dst, i
     return cudaGetLastError();
 }
 
+// ── split-K reduction ────────────────────────────────────────────────────────
+// C[r, c] = Σ_{s = 0..S-1} ws[s][r][c] (fp32, in split order, from 0), stored as fp16 (round
+// to nearest) or fp32. ws holds S row-major M × N partials. One thread per 4 consecutive
+// columns of a row; 16-byte loads when N % 4 == 0.
+__global__ void splitk_reduce(const float *__restrict__ ws, int S, long long stride, int M, int N,
+                              void *__restrict__ C, long long ldc, int f32_out) {
+    const int groups = (N + 3) / 4;
+    const long long total = (long long)M * groups;
+    const bool vec = (N % 4) == 0;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / groups;
+        const int c0 = (int)(i - r * groups) * 4;
+        const float *src = ws + r * N + c0;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < S; ++s) {
+            const float *p = src + (long long)s * stride;
+            if (vec) {
+                const float4 v = *reinterpret_cast<const float4 *>(p);
+                acc[0] += v.x;
+                acc[1] += v.y;
+                acc[2] += v.z;
+                acc[3] += v.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (c0 + e < N)
+                        acc[e] += p[e];
+            }
+        }
+        if (f32_out) {
+            float *crow = static_cast<float *>(C) + r * ldc;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (c0 + e < N)
+                    crow[c0 + e] = acc[e];
+        } else {
+            __half *crow = static_cast<__half *>(C) + r * ldc;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (c0 + e < N)
+                    crow[c0 + e] = __float2half_rn(acc[e]);
+        }
+    }
+}
+
+cudaError_t launch_splitk_reduce(const float *ws, int S, int M, int N, void *C, long long ldc, bool f32_out,
+                                 int num_sms, cudaStream_t s) {
+    const long long total = (long long)M * ((N + 3) / 4);
+    if (total == 0)
+        return cudaSuccess;
+    const int threads = 256;
+    const int blocks = (int)std::min<long long>((total + threads - 1) / threads, (long long)num_sms * 8);
+    splitk_reduce<<<blocks, threads, 0, s>>>(ws, S, (long long)M * N, M, N, C, ldc, f32_out ? 1 : 0);
+    return cudaGetLastError();
+}
+
 // ── kernel launch ────────────────────────────────────────────────────────────
 template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> struct Inst {
     static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
@@ -607,7 +684,7 @@ inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
 // slots of the chunked pair-tile accumulation, then the words zeroed before every launch
 // (stream-K ready flags, the run-time tile counter).
 struct WsLayout {
-    size_t a_off = 0, b_off = 0, part_off = 0, slot_off = 0, flag_off = 0, ctr_off = 0;
+    size_t a_off = 0, b_off = 0, part_off = 0, slot_off = 0, split_off = 0, flag_off = 0, ctr_off = 0;
     size_t flag_bytes = 0, total = 0;
     bool promote_slots = false;
 };
@@ -621,15 +698,18 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
     // One 128 × BN fp32 running sum per CTA when the pair tile's K range has several chunks.
     w.promote_slots = p.promote && p.bn == 512 && p.promote_kb < p.num_kb;
     const size_t slot = w.promote_slots ? (size_t)grid * 128 * (size_t)p.bn * sizeof(float) : 0;
+    // Split-K: one fp32 M × N partial per split.
+    const size_t split = p.splits > 1 ? round_up_256((size_t)p.splits * M * N * sizeof(float)) : 0;
     const size_t words = sk_slots + (p.dyn ? 1 : 0);
     w.a_off = 0;
     w.b_off = a;
     w.part_off = a + b;
     w.slot_off = a + b + part;
-    w.flag_off = a + b + part + slot;
+    w.split_off = a + b + part + slot;
+    w.flag_off = a + b + part + slot + split;
     w.ctr_off = w.flag_off + sk_slots * sizeof(unsigned);
     w.flag_bytes = words ? round_up_256(words * sizeof(unsigned)) : 0;
-    w.total = a + b + part + slot + w.flag_bytes;
+    w.total = a + b + part + slot + split + w.flag_bytes;
     return w;
 }
 
@@ -736,6 +816,7 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     unsigned *sk_flags = nullptr;
     float *promote_slots = nullptr;
     unsigned *sched_ctr = nullptr;
+    float *split_ws = nullptr;
     if (wl.total) {
         char *base = nullptr;
         if (src == WsSource::Pool) {
@@ -769,6 +850,8 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
         }
         if (wl.promote_slots)
             promote_slots = reinterpret_cast<float *>(base + wl.slot_off);
+        if (p.splits > 1)
+            split_ws = reinterpret_cast<float *>(base + wl.split_off);
         if (p.dyn)
             sched_ctr = reinterpret_cast<unsigned *>(base + wl.ctr_off);
         if (e == cudaSuccess && wl.flag_bytes)
@@ -785,7 +868,7 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     const uint32_t b_box_rows = (uint32_t)(p.bn / p.cta_group);
     bool ok = get_map(ma, A_use, (uint64_t)Kp, (uint64_t)M, (uint64_t)Kp, 64u, 128u, dev) &&
               get_map(mb, B_use, (uint64_t)Kp, (uint64_t)N, (uint64_t)Kp, 64u, b_box_rows, dev);
-    if (ok && (p.epi == kEpiTmaF16 || p.epi == kEpiTmaF16Peers))
+    if (ok && p.splits == 1 && (p.epi == kEpiTmaF16 || p.epi == kEpiTmaF16Peers))
         ok = get_map(mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)N, 64u, 32u, dev);
     if (!ok) {
         if (owned)
@@ -814,8 +897,24 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     for (int i = 0; i < num_peers; ++i)
         args.peers[i] = peers[i];
     args.mc = c_multicast;
+    args.splits = 1;
 
-    e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+    if (p.splits > 1) {
+        // Split-K: the kernel writes each split's fp32 partial into the workspace (row-major,
+        // ld = N), then the reduction kernel adds the splits in order and writes C.
+        Plan pk = p;
+        pk.epi = kEpiDirectF32;
+        args.C = split_ws;
+        args.ldc = N;
+        args.c_vec_ok = (N % 4 == 0);
+        args.splits = p.splits;
+        args.split_stride = (long long)M * N;
+        e = dispatch(pk, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+        if (e == cudaSuccess)
+            e = launch_splitk_reduce(split_ws, p.splits, M, N, C, N, f32_out, di->num_sms, s);
+    } else {
+        e = dispatch(p, dev, max_clusters, false, &ma, &mb, &mc, &args, grid, s);
+    }
     if (owned) {
         const cudaError_t f = cudaFreeAsync(owned, s);
         if (e == cudaSuccess)
@@ -984,17 +1083,17 @@ void vg_shard_rows(long long M, int world, int rank, long long *row0, long long 
 }
 
 int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, int group_m,
-                  int num_kb, int *out, int max_units) {
+                  int num_kb, int splits, int *out, int max_units) {
     if (worker < 0 || workers <= 0 || worker >= workers || num_m <= 0 || num_n <= 0 ||
-        group_m <= 0 || num_kb <= 0 || max_units < 0)
+        group_m <= 0 || num_kb <= 0 || max_units < 0 || splits < 1 || (stream_k && splits != 1))
         return -1;
     vg::UnitIter it;
-    it.init(stream_k != 0, worker, workers, num_m, num_n, group_m, num_kb);
+    it.init(stream_k != 0, worker, workers, num_m, num_n, group_m, num_kb, splits);
     vg::WorkUnit u;
     int n = 0;
     while (it.next(u)) {
         if (out && n < max_units) {
-            int *o = out + 7 * n;
+            int *o = out + 8 * n;
             o[0] = u.tile_m;
             o[1] = u.tile_n;
             o[2] = u.kb0;
@@ -1002,6 +1101,7 @@ int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, i
             o[4] = u.kind;
             o[5] = u.first_contrib;
             o[6] = u.last_contrib;
+            o[7] = u.split;
         }
         ++n;
     }
@@ -1027,10 +1127,10 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
                                 mode == 2);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[18] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
+    const int vals[19] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
                           p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
                           p.grid,      p.persistent,  p.bn,          p.version, p.stream_k,
-                          p.promote,   p.dyn,         p.promote_kb};
+                          p.promote,   p.dyn,         p.promote_kb,  p.splits};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }
