@@ -795,9 +795,14 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     if (e != cudaSuccess)
         return e;
 
+    // The kernel that runs: split-K writes fp32 partials (its plan's epilogue names the
+    // reduction kernel's output).
+    Plan pk = p;
+    if (p.splits > 1)
+        pk.epi = kEpiDirectF32;
     // Occupancy-limited cluster count for the persistent pair kernel.
     int max_clusters = 0;
-    e = dispatch(p, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
+    e = dispatch(pk, dev, max_clusters, true, nullptr, nullptr, nullptr, nullptr, 0, s);
     if (e != cudaSuccess)
         return e;
     int grid = p.grid;
@@ -902,8 +907,6 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     if (p.splits > 1) {
         // Split-K: the kernel writes each split's fp32 partial into the workspace (row-major,
         // ld = N), then the reduction kernel adds the splits in order and writes C.
-        Plan pk = p;
-        pk.epi = kEpiDirectF32;
         args.C = split_ws;
         args.ldc = N;
         args.c_vec_ok = (N % 4 == 0);
