@@ -30,8 +30,7 @@ def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
                              "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
-                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11",
-                             "VibeGEMM B200 v12"]
+                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -145,17 +144,17 @@ def test_plan_of_run_time_tiles_and_chunks(vg):
 
 
 def test_plan_of_split_k(vg):
-    """v12: K splits that give every pair slot a unit, >= 8 k-blocks each, and chains of at
+    """v11: K splits that give every pair slot a unit, >= 8 k-blocks each, and chains of at
     most 64 k-blocks from K = 16384 on; one split (plain v2) when the grid is already full."""
-    p = vg.plan(12, 256, 2048, 32768, 256, 256, 256)
+    p = vg.plan(11, 256, 2048, 32768, 256, 256, 256)
     assert p["splits"] == 9 and p["epilogue"] == "splitk_f16" and p["grid"] == 2 * 72
-    assert vg.plan(12, 256, 2048, 32768, 256, 256, 256, f32_out=True)["epilogue"] == "direct_f32"
-    assert vg.plan(12, 256, 2048, 1024, 256, 256, 256)["splits"] == 2   # 16 k-blocks: 2 x 8
-    full = vg.plan(12, 8192, 8192, 8192, 256, 256, 256)
+    assert vg.plan(11, 256, 2048, 32768, 256, 256, 256, f32_out=True)["epilogue"] == "direct_f32"
+    assert vg.plan(11, 256, 2048, 1024, 256, 256, 256)["splits"] == 2   # 16 k-blocks: 2 x 8
+    full = vg.plan(11, 8192, 8192, 8192, 256, 256, 256)
     assert full["splits"] == 1 and full["epilogue"] == "tma_f16"
-    assert vg.plan(12, 8192, 8192, 32768, 256, 256, 256)["splits"] == 8  # chains <= 4096
+    assert vg.plan(11, 8192, 8192, 32768, 256, 256, 256)["splits"] == 8  # chains <= 4096
     with pytest.raises(vg.VibeGemmError):   # no fused all-gather form
-        vg.plan(12, 256, 2048, 32768, 256, 256, 256, allgather=True)
+        vg.plan(11, 256, 2048, 32768, 256, 256, 256, allgather=True)
 
 
 def test_plan_rejects_bad_input(vg):

@@ -105,8 +105,8 @@ struct GemmArgs {
 constexpr int kSchedDepth = 4;
 
 template <int CG, int BN_> struct TileCfg {
-    static_assert(BN_ == 256 || BN_ == 192 || (BN_ == 512 && CG == 2),
-                  "tile: 128x256, 128x192, pair 256x256, pair 256x192 or pair 256x512");
+    static_assert(BN_ == 256 || (BN_ == 192 && CG == 1) || (BN_ == 512 && CG == 2),
+                  "tile: 128x256, 128x192, pair 256x256 or pair 256x512");
     static constexpr int BM = 128;          // accumulator rows per CTA (TMEM lanes)
     static constexpr int BN = BN_;          // tile columns
     static constexpr int BK = 64;           // fp16 per 128-B swizzle row

@@ -31,9 +31,7 @@
 //       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
 //   v10 v9 without the chunking: one accumulation chain per output, as cuBLAS (the
 //       fastest long-K kernel; bit-identical to v3/v6).
-//   v11 CTA pair with a 256×192 tile (each CTA loads 96 rows of B), 6-stage ring: for
-//       grids that fill one wave, 30 % fewer L2→SMEM bytes per FLOP than 128×192 (v5).
-//   v12 split-K over v2's pair tile for grids with few tiles and long K: tile × K-split
+//   v11 split-K over v2's pair tile for grids with few tiles and long K: tile × K-split
 //       units fill the pairs, each writes an fp32 partial, and a reduction kernel adds the
 //       splits in order and stores C (deterministic; every output's chain is K / splits).
 //   auto (the default entry point) picks one of them per shape (select_version).
@@ -87,8 +85,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true, true},
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
-    {"VibeGEMM B200 v11", 2, 192, 6, true, true, 8},
-    {"VibeGEMM B200 v12", 2, 256, 6, true, true, 8, false, false, false, true},
+    {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -661,8 +658,6 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
                                                           args, grid, s);
     if (!p.stream_k && p.cta_group == 2 && p.bn == 256 && p.stages == 6)
         return dispatch_epi<2, 256, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
-    if (p.cta_group == 2 && p.bn == 192 && p.stages == 6) // v11
-        return dispatch_epi<2, 192, 6>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 5)
         return dispatch_epi<1, 192, 5>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.dyn && p.promote && p.cta_group == 2 && p.bn == 512 && p.stages == 4) // v9
