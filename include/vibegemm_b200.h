@@ -52,9 +52,9 @@ int vg_b200_gemm_f16_version(int version, const void *A, const void *B, void *C,
  * instead and never calls cudaMalloc, cudaMallocAsync, cudaFree or an allocating library.
  *   - Limit: the call's workspace must fit in 32 MiB: a padded copy of each operand that
  *     needs one (M * roundup(K, 8) * 2 bytes for A, N * roundup(K, 8) * 2 bytes for B), plus
- *     for small grids that use stream-K scheduling the fp32 partial tiles and their flags
- *     (at most 148 * 128 KB = 18.5 MiB), plus 256 bytes for the tile counter of the
- *     versions that claim tiles at run time. Larger workspaces return
+ *     for small grids whose K range is split the fp32 partials of every split (splits *
+ *     M * N * 4 bytes; about 19 MiB at most for the grids the per-shape choice splits), plus
+ *     256 bytes for the tile counter of the versions that claim tiles at run time. Larger workspaces return
  *     VG_ERROR_NOALLOC_SCRATCH_LIMIT and launch nothing. Problems that need none of these
  *     have no size limit.
  *   - The 32 MiB belong to the library's device code. With CUDA's lazy module loading

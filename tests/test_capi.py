@@ -91,7 +91,7 @@ def test_plan_aligned_square(vg):
     ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
     ((1000, 3000, 8192), 7),     # same tiles, long K: the fifth stage pays
     ((512, 512, 512), 5),
-    ((256, 2048, 32768), 4),     # 8 pair tiles, 512 k-blocks each: stream-K over 74 pairs
+    ((256, 2048, 32768), 11),    # 8 pair tiles, 512 k-blocks each: split-K over 74 pairs
     ((512, 8192, 32768), 8),     # 64 pair tiles on 74 pairs: v2's tile, chunked accumulation
     ((1000, 3000, 32768), 8),    # long K on an under-filled grid: chains split (v8, not v7)
     ((512, 8192, 16384), 8), ((512, 8192, 8192), 2),
@@ -172,9 +172,10 @@ def test_gemm_rejects_cpu_tensors(vg):
 
 
 def test_allgather_plan_never_uses_stream_k(vg):
-    """The fused all-gather epilogue has no stream-K form: its per-shape choice skips v4
-    (a 501-row shard of 1001×1024×4099 would otherwise pick it) and an explicit v4 is refused."""
-    assert vg.plan(-1, 501, 1024, 4099, 256, 256, 256)["version"] == 4
+    """The fused all-gather epilogue has no stream-K or split-K form: its per-shape choice
+    skips them (a 501-row shard of 1001×1024×4099 would otherwise split K) and an explicit
+    v4 is refused."""
+    assert vg.plan(-1, 501, 1024, 4099, 256, 256, 256)["version"] == 11
     p = vg.plan(-1, 501, 1024, 4099, 256, 256, 256, allgather=True)
     assert p["version"] != 4 and p["stream_k"] == 0 and p["epilogue"] == "tma_f16_peers"
     with pytest.raises(vg.VibeGemmError):

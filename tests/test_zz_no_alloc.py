@@ -89,17 +89,18 @@ def test_noalloc_needs_no_scratch_when_aligned(vg, orc):
     assert np.array_equal(ref, new)
 
 
-def test_noalloc_stream_k_partials_live_in_the_array(vg, orc):
-    """A grid too small for one wave with long K: the per-shape choice is stream-K (v4), whose
-    fp32 partial tiles and ready flags then sit in the fixed array instead of the pool. Two
-    calls in a row (the second finds the first one's partials and flags still there) must
-    both equal the default entry point bit for bit (same kernel, same contributor order),
-    and the result meets the long-K bound against the fp64 product on sampled rows."""
+def test_noalloc_split_k_partials_live_in_the_array(vg, orc):
+    """A grid too small for one wave with long K: the per-shape choice splits K (v11), whose
+    fp32 partials of every split then sit in the fixed array instead of the pool before the
+    reduction kernel adds them. Two calls in a row (the second finds the first one's partials
+    still there) must both equal the default entry point bit for bit (same splits, same order
+    of additions), and the result meets the long-K bound against the fp64 product on sampled
+    rows."""
     import torch
     f_noalloc, f_default = _c_abi(vg)
     M, N, K = 256, 2048, 16384
     p = vg.plan(-1, M, N, K, 256, 256, 256)
-    assert p["stream_k"] == 1 and p["pad_a"] == 0 and p["pad_b"] == 0, p
+    assert p["version"] == 11 and p["splits"] > 1 and p["pad_a"] == 0 and p["pad_b"] == 0, p
     A, B = orc.make_inputs(M, N, K)
     dA, dB = to_dev(A), to_dev(B)
     s = torch.cuda.current_stream().cuda_stream

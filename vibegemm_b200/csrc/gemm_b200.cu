@@ -120,7 +120,7 @@ int promote_chunk_kb(int version_promote_kind, int num_kb, int Kp) {
 // (v7: one staging box per epilogue warp; +14 % at 1000×3000×8192, -3..5 % at K <= 2048,
 // where the shorter epilogue matters more) and stream-K (v4, only for long K over few
 // tiles: its fp32 fix-up costs about 28 k-blocks per split tile).
-int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true) {
+int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
@@ -146,31 +146,33 @@ int select_version(int M, int N, int K, int num_sms, bool allow_stream_k = true)
     if (t2 >= pairs)
         return 2;
     // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
-    // (v1), pair 256×256 (v2), 128×192 (v5) and stream-K over pair tiles (v4), whose split
-    // tiles pay a fix-up of about 28 k-blocks (partials out, owner reads them back, the
-    // flag reset). Stream-K wins only when K is long and the tiles are few (e.g.
-    // 256×2048×32768); it also splits each output's accumulation chain, which makes it
-    // the more accurate choice there.
+    // (v1), pair 256×256 (v2), 128×192 (v5) and a K split over pair tiles (estimated as
+    // stream-K, v4, whose split tiles pay a fix-up of about 28 k-blocks: partials out, owner
+    // reads them back, the flag reset). Splitting K wins only when K is long and the tiles are
+    // few (e.g. 256×2048×32768); it also splits each output's accumulation chain.
     const long long kb = ceil_div_i(K, 64);
     const long long t1 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 256);
     const long long t5 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 192);
     const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 * kb / 1.1;
     const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 * kb / 1.0;
     const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 * kb / 0.95;
-    // (stream-K only for grids at most half full: a single wave on most pairs runs at a
-    // higher clock under the power cap than the estimate credits, e.g. 512×8192×32768
-    // measured v2 1320 vs v4 1047 TFLOP/s)
-    const double e4 = (allow_stream_k && 2 * t2 <= pairs)
+    // (K split over the pairs only for grids at most half full: a single wave on most pairs
+    // runs at a higher clock under the power cap than the estimate credits, e.g.
+    // 512×8192×32768 measured v2 1320 vs v4 1047 TFLOP/s.) The estimate is stream-K's; where it
+    // wins, split-K (v11, fp32 partials added in split order by a reduction kernel) was measured
+    // faster than stream-K on every such shape: 256×2048×32768 754 vs 566 TFLOP/s,
+    // 1024×1024×16384 856 vs 735, 256×4096×8192 590 vs 478, 1024×2048×8192 864 vs 801.
+    const double e4 = (allow_split && 2 * t2 <= pairs)
                           ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
                           : 1e300;
     const double e7 = e5 * (kb >= 64 ? 0.88 : 1.04);
     if (split_chains)
-        return e4 <= e2 * 1.1 ? 4 : 8;
+        return e4 <= e2 * 1.1 ? 11 : 8;
     const double best = std::min({e1, e2, e4, e5, e7});
     if (e7 == best)
         return 7;
     if (e4 == best)
-        return 4;
+        return 11;
     if (e5 == best)
         return 5;
     return e2 <= e1 ? 2 : 1;
@@ -221,7 +223,7 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
               int num_sms, int max_clusters, Plan &p, bool peers = false) {
     if (M < 0 || N < 0 || K < 0 || num_sms <= 0)
         return cudaErrorInvalidValue;
-    if (version == kAutoVersion) // the fused all-gather epilogue has no stream-K form
+    if (version == kAutoVersion) // the fused all-gather epilogue has no stream-K / split-K form
         version = select_version(M, N, K, num_sms, !peers);
     if (version < 0 || version >= kNumVersions)
         return cudaErrorInvalidValue;
@@ -709,7 +711,8 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
 }
 
 // ── workspaces ───────────────────────────────────────────────────────────────
-// Workspace of vg_b200_gemm_f16_noalloc (K-padded operands, stream-K partials and flags):
+// Workspace of vg_b200_gemm_f16_noalloc (K-padded operands, stream-K or split-K partials,
+// stream-K flags and the tile counter):
 // a fixed array in the module's device memory instead of the stream-ordered pool. A GPU
 // reserves these kNoAllocScratchBytes when this module is first loaded on it (with lazy
 // module loading: the first GEMM call on that device) and holds them until the process
