@@ -31,6 +31,7 @@
 //       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
 //   v10 v9 without the chunking: one accumulation chain per output, as cuBLAS (the
 //       fastest long-K kernel; bit-identical to v3/v6).
+//   v12 split-K over v1's 128×256 single-CTA tile (units fill the SMs instead of the pairs).
 //   v11 split-K over v2's pair tile for grids with few tiles and long K: tile × K-split
 //       units fill the pairs, each writes an fp32 partial, and a reduction kernel adds the
 //       splits in order and stores C (deterministic; every output's chain is K / splits).
@@ -86,6 +87,7 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
+    {"VibeGEMM B200 v12", 1, 256, 4, true, true, 8, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -261,9 +263,9 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.promote_kb = v.promote ? promote_chunk_kb(v.cta_group == 2 && v.bn == 512 ? 2 : 1, p.num_kb, p.Kp)
                              : p.num_kb;
     if (v.split_k) {
-        // Enough K splits to give every pair slot a unit (one wave), at least 8 k-blocks per
-        // split, and from K = kPromoteMinK on chains of at most kPromoteKb k-blocks.
-        const int slots = std::max(1, max_clusters);
+        // Enough K splits to give every slot (pair or SM) a unit (one wave), at least 8
+        // k-blocks per split, and from K = kPromoteMinK on chains of at most kPromoteKb k-blocks.
+        const int slots = (v.cta_group == 2) ? std::max(1, max_clusters) : num_sms;
         long long S = std::max(1LL, slots / std::max(1LL, tiles));
         S = std::min<long long>(S, std::max(1, p.num_kb / 8));
         if (p.Kp >= kPromoteMinK)
