@@ -30,8 +30,7 @@ def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
                              "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
-                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11",
-                             "VibeGEMM B200 v12"]
+                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -156,9 +155,6 @@ def test_plan_of_split_k(vg):
     assert vg.plan(11, 8192, 8192, 32768, 256, 256, 256)["splits"] == 8  # chains <= 4096
     with pytest.raises(vg.VibeGemmError):   # no fused all-gather form
         vg.plan(11, 256, 2048, 32768, 256, 256, 256, allgather=True)
-    # v12: the same over single-CTA 128x256 tiles, whose units fill the SMs
-    p12 = vg.plan(12, 1024, 2048, 4096, 256, 256, 256)
-    assert (p12["cta_group"], p12["splits"], p12["grid"]) == (1, 2, 128)
 
 
 def test_plan_rejects_bad_input(vg):

@@ -31,7 +31,6 @@
 //       accumulation whose fp32 running sum lives in a per-CTA slot in global memory.
 //   v10 v9 without the chunking: one accumulation chain per output, as cuBLAS (the
 //       fastest long-K kernel; bit-identical to v3/v6).
-//   v12 split-K over v1's 128×256 single-CTA tile (units fill the SMs instead of the pairs).
 //   v11 split-K over v2's pair tile for grids with few tiles and long K: tile × K-split
 //       units fill the pairs, each writes an fp32 partial, and a reduction kernel adds the
 //       splits in order and stores C (deterministic; every output's chain is K / splits).
@@ -87,7 +86,6 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
-    {"VibeGEMM B200 v12", 1, 256, 4, true, true, 8, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
