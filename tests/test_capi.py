@@ -91,6 +91,7 @@ def test_plan_aligned_square(vg):
     ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
     ((1000, 3000, 8192), 7),     # same tiles, long K: the fifth stage pays
     ((512, 512, 512), 5),
+    ((2048, 2048, 4096), 1),     # one wave either way; at K = 4096 single CTAs beat pairs
     ((256, 2048, 32768), 11),    # 8 pair tiles, 512 k-blocks each: split-K over 74 pairs
     ((512, 8192, 32768), 8),     # 64 pair tiles on 74 pairs: v2's tile, chunked accumulation
     ((1000, 3000, 32768), 8),    # long K on an under-filled grid: chains split (v8, not v7)

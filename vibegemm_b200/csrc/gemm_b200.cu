@@ -150,12 +150,15 @@ int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     // stream-K, v4, whose split tiles pay a fix-up of about 28 k-blocks: partials out, owner
     // reads them back, the flag reset). Splitting K wins only when K is long and the tiles are
     // few (e.g. 256×2048×32768); it also splits each output's accumulation chain.
+    // Each wave also pays a fixed cost (prologue, last epilogue), in k-blocks: ~10 for single
+    // CTAs and ~30 for pairs, whose main loop runs ~1.2x faster per SM (fitted to one-wave
+    // runs: 2048×2048×4096 v1 1270 vs v2 1190 TFLOP/s, 512×8192×32768 v2 1335 vs v1 1161).
     const long long kb = ceil_div_i(K, 64);
     const long long t1 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 256);
     const long long t5 = (long long)ceil_div_i(M, 128) * ceil_div_i(N, 192);
-    const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 * kb / 1.1;
-    const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 * kb / 1.0;
-    const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 * kb / 0.95;
+    const double e2 = (double)((t2 + pairs - 1) / pairs) * 256 * (kb + 30) / 1.2;
+    const double e1 = (double)((t1 + num_sms - 1) / num_sms) * 256 * (kb + 10) / 1.0;
+    const double e5 = (double)((t5 + num_sms - 1) / num_sms) * 192 * (kb + 10) / 0.95;
     // (K split over the pairs only for grids at most half full: a single wave on most pairs
     // runs at a higher clock under the power cap than the estimate credits, e.g.
     // 512×8192×32768 measured v2 1320 vs v4 1047 TFLOP/s.) The estimate is stream-K's; where it
@@ -163,7 +166,7 @@ int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     // faster than stream-K on every such shape: 256×2048×32768 754 vs 566 TFLOP/s,
     // 1024×1024×16384 856 vs 735, 256×4096×8192 590 vs 478, 1024×2048×8192 864 vs 801.
     const double e4 = (allow_split && 2 * t2 <= pairs)
-                          ? (double)((t2 * kb + pairs - 1) / pairs + 28) * 256 / 1.1
+                          ? (double)((t2 * kb + pairs - 1) / pairs + 28 + 10) * 256 / 1.1
                           : 1e300;
     const double e7 = e5 * (kb >= 64 ? 0.88 : 1.04);
     if (split_chains)
