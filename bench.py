@@ -486,8 +486,8 @@ def run_b200(args) -> None:
         ms32 = max_over_ranks(run_timed(gemm32, steps32, 3, "sharded32k gemm"))
         tf32 = flop32 / (ms32 * 1e-3) / 1e12
         # Beside it, on the same shards: cuBLAS, and v10 (run-time tile claims with ONE
-        # accumulation chain per output, as cuBLAS; the default, v8, splits the chains at this
-        # K so that the bounded relative error stays within 1e-2).
+        # accumulation chain per output, as cuBLAS; the default splits the chains at this K
+        # so that the bounded relative error stays within 1e-2).
         C32b = torch.empty_like(C32)
 
         def cublas32():

@@ -81,9 +81,10 @@ def test_plan_aligned_square(vg):
 
 
 @pytest.mark.parametrize("shape,want", [
-    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 8),
+    ((8192, 8192, 8192), 3), ((32768, 32768, 32768), 9),
     ((4096, 14336, 4096), 2),    # 448 256x512 tiles = 6.05 waves; 896 256x256 tiles waste less
-    ((16384, 16384, 16384), 8), ((4096, 32768, 32768), 8),   # long K: chunks summed in TMEM
+    ((16384, 16384, 16384), 9), ((4096, 32768, 32768), 9),   # long K: chunks, sums in registers
+    ((2560, 4096, 32768), 8),    # 80 256x512 tiles = 2 waves vs 160 256x256 = 3: sums in TMEM
     ((8192, 8192, 12288), 3),    # below the promotion threshold: one chain per output
     ((4096, 4096, 14336), 3),
     ((8191, 8193, 4099), 3),     # 7.4 vs 14.3 waves: estimates within 1.5 %, v3's data saving wins
@@ -135,12 +136,12 @@ def test_plan_of_run_time_tiles_and_chunks(vg):
     assert (p10["dyn"], p10["promote"], p10["promote_kb"]) == (1, 0, 512)
     assert vg.plan(8, 8192, 8192, 8192, 256, 256, 256)["promote_kb"] == 64
     assert vg.plan(3, 8192, 8192, 8192, 256, 256, 256)["dyn"] == 0
-    # v8 (the long-K default) claims tiles at run time too; the fused all-gather's choice for
-    # a long-K shard promotes as well
+    # v8 (the long-K choice on smaller grids) claims tiles at run time too; the fused
+    # all-gather's choice for a long-K shard promotes as well
     p8 = vg.plan(8, 32768, 32768, 32768, 256, 256, 256)
     assert (p8["dyn"], p8["promote"], p8["promote_kb"], p8["tile_n"]) == (1, 1, 64, 256)
     p = vg.plan(-1, 4096, 32768, 32768, 256, 256, 256, allgather=True)
-    assert p["version"] == 8 and p["epilogue"] == "tma_f16_peers"
+    assert p["version"] == 9 and p["epilogue"] == "tma_f16_peers"
     assert vg.plan(-1, 512, 8192, 32768, 256, 256, 256, allgather=True)["version"] == 8
 
 

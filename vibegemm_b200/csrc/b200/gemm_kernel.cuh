@@ -89,9 +89,6 @@ struct GemmArgs {
     float *sk_partials;
     unsigned *sk_flags;
     int promote_kb; // PROMOTE kernels: k-blocks per accumulation chunk
-    // PROMOTE with the 256×512 pair tile: one running-sum slot of 128 × 512 fp32 per CTA
-    // (column-quad major), used only when a tile has more than one chunk.
-    float *promote_slots;
     // DYN kernels: tile claim counter, zeroed before the launch.
     unsigned *sched_ctr;
     // Split-K (fp32 output only): the K range is cut into `splits` parts; the partial of split
@@ -104,9 +101,14 @@ struct GemmArgs {
 // claimed tile to the other roles of the pair.
 constexpr int kSchedDepth = 4;
 
-template <int CG, int BN_> struct TileCfg {
+// RSUM: the pair 256×512 tile with chunked accumulation whose running sums live in the
+// epilogue warps' registers (three warpgroups: producer / MMA / two idle warps, then eight
+// epilogue warps with most of the register file).
+template <int CG, int BN_, bool RSUM_ = false> struct TileCfg {
     static_assert(BN_ == 256 || (BN_ == 192 && CG == 1) || (BN_ == 512 && CG == 2),
                   "tile: 128x256, 128x192, pair 256x256 or pair 256x512");
+    static_assert(!RSUM_ || (CG == 2 && BN_ == 512), "register sums: the pair 256x512 tile");
+    static constexpr bool RSUM = RSUM_;
     static constexpr int BM = 128;          // accumulator rows per CTA (TMEM lanes)
     static constexpr int BN = BN_;          // tile columns
     static constexpr int BK = 64;           // fp16 per 128-B swizzle row
@@ -129,9 +131,15 @@ template <int CG, int BN_> struct TileCfg {
     // use 8: their epilogue chunks take ~1.6-2.5x as long as a single CTA's (measured), and
     // splitting a tile's chunks over two warp groups gained 3-8 % on short-K and unaligned
     // shapes; single CTAs keep 4 (8 cost them 2-3 %).
-    static constexpr int EPI_WARPS = (CG == 2) ? VG_EPI_WARPS_PAIR : 4;
+    static constexpr int EPI_WARPS = RSUM ? 8 : (CG == 2) ? VG_EPI_WARPS_PAIR : 4;
     static constexpr int EPI_GROUPS = EPI_WARPS / 4;
-    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int EPI_WARP0 = RSUM ? 4 : 2; // first epilogue warp
+    static constexpr int THREADS = 32 * EPI_WARP0 + 32 * EPI_WARPS;
+    // RSUM register budgets per thread (launched with 168 = 65536 / 384, rounded down to a
+    // multiple of 8): warpgroup 0 gives up 128 registers per thread, which the two epilogue
+    // warpgroups take, 64 each (40 + 2 * 232 = 3 * 168).
+    static constexpr int RSUM_REGS_LOW = 40;
+    static constexpr int RSUM_REGS_HIGH = 232;
     // Chunks per TMEM release unit: a whole buffer, or one 256-column half of the BN = 512
     // accumulator.
     static constexpr int CHUNKS_PER_UNIT = (ACC_BUFS == 2) ? NCHUNK : 4;
@@ -182,9 +190,13 @@ __device__ unsigned int vg_status_word;
 #define VG_EPI_BACKOFF_NS 0
 #endif
 
-__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                       unsigned long long timeout_ns, unsigned code,
-                                       unsigned backoff_ns) {
+// The slow path of a bounded wait. Kernels that shift registers between warpgroups
+// (setmaxnreg) take it inlined: a called function has one register allocation, which cannot
+// serve warpgroups with different budgets (ptxas refuses such a kernel); the others share one
+// out-of-line copy.
+__device__ __forceinline__ bool wait_slow_inline(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                                 unsigned long long timeout_ns, unsigned code,
+                                                 unsigned backoff_ns) {
     const uint64_t t0 = ptx::global_timer_ns();
     for (uint32_t it = 1;; ++it) {
         // Suspend in hardware (up to ~0.1 ms per probe) rather than spin.
@@ -204,12 +216,22 @@ __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile i
     }
 }
 
+__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                       unsigned long long timeout_ns, unsigned code,
+                                       unsigned backoff_ns) {
+    return wait_slow_inline(bar, parity, abort_flag, timeout_ns, code, backoff_ns);
+}
+
+template <bool INLINE = false>
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                          unsigned long long timeout_ns, unsigned code,
                                          unsigned backoff_ns = 0) {
     if (ptx::mbar_try_wait(bar, parity))
         return true;
-    return wait_slow(bar, parity, abort_flag, timeout_ns, code, backoff_ns);
+    if constexpr (INLINE)
+        return wait_slow_inline(bar, parity, abort_flag, timeout_ns, code, backoff_ns);
+    else
+        return wait_slow(bar, parity, abort_flag, timeout_ns, code, backoff_ns);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(uint32_t lo_bits, uint32_t hi_bits) {
@@ -242,18 +264,20 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
     }
 }
 
-// PROMOTE: each tile's K range is cut into chunks of args.promote_kb k-blocks; every chunk
-// is accumulated by the tensor cores from zero, and the epilogue warps add it in fp32
-// (round to nearest) into a running sum. Each output then sums short tensor-core chains
-// instead of one long one (the tensor cores' accumulation rounds toward zero, an error that
-// grows with the chain). With two TMEM buffers (BN = 256) the running sum is TMEM buffer 1
-// and the MMA waits while a chunk is added in. With the 256×512 pair tile, which fills TMEM,
-// the running sum is a per-CTA slot in global memory (args.promote_slots, L2-resident): the
-// epilogue loads each half of a finished chunk into registers, hands the half back to the
-// MMA at once and then stores it (first chunk) or adds it (later chunks: red.add in L2, no
-// read latency) into the slot, so the next chunk's MMAs overlap the adds; the last chunk
-// adds the slot into its values on the way to the C store. Every slot element is only ever
-// touched by one thread, so the adds happen in chunk order (deterministic). No stream-K.
+// PROMOTE: each tile's K range is cut into chunks of args.promote_kb k-blocks, and the
+// epilogue warps carry a running sum across them in fp32 arithmetic (round to nearest). Each
+// output then sums short tensor-core chains instead of one long one (the tensor cores'
+// accumulation rounds toward zero, an error that grows with the chain). With two TMEM buffers
+// (BN = 256) every chunk is accumulated from zero in buffer 0 and added into the running sum
+// in TMEM buffer 1. The 256×512 pair tile fills TMEM, so its running sums live in the
+// registers of the eight epilogue warps (RSUM, three warpgroups: 256 sums per thread as 128
+// bf16 pairs, with the register file shifted to the epilogue by setmaxnreg): at a chunk
+// boundary each thread forms s = sum + chunk, keeps sum = bf16(s) and writes the remainder
+// s - sum (exact in fp32) back into TMEM, on which the next chunk's MMAs accumulate. The sum
+// is therefore carried without loss; the only roundings outside the tensor cores are the
+// fp32 additions. The MMA issuer waits while a half is read out and written back (the other
+// half's MMAs run ahead meanwhile). Every element is only ever touched by one thread, in
+// chunk order (deterministic). No stream-K.
 //
 // DYN (CTA pairs): tiles are claimed at run time instead of by the static walk. Each pair
 // starts with tile cluster_id; afterwards the leader CTA's producer claims the next tile
@@ -263,13 +287,14 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
 // finish early take more tiles, as with hardware-placed pairs, while the epilogue of one
 // tile still overlaps the next tile's main loop.
 template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false, bool DYN = false>
-__global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
+__global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREADS), 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-    using T = TileCfg<CG, BN>;
+    using T = TileCfg<CG, BN, PROMOTE && BN == 512>;
     using L = SmemLayout<CG, BN, STAGES, EPI>;
+    static_assert(L::T::EPI_WARPS == T::EPI_WARPS, "shared-memory layout sized for these warps");
     static_assert(!PROMOTE || ((T::ACC_BUFS == 2 || CG == 2) && !SK),
                   "PROMOTE: two TMEM buffers or the pair tile, no stream-K");
     static_assert(!DYN || (CG == 2 && !SK), "DYN: CTA pairs, no stream-K");
@@ -366,7 +391,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         t = (ring_seq == 0) ? cluster_id : num_clusters + static_cast<int>(atomicAdd(args.sched_ctr, 1u));
         if (t > total_tiles)
             t = total_tiles;
-        if (!wait_bar(sempty_bar(i), ph ^ 1u, abort_flag, tmo, kStatusTimeoutProducer))
+        if (!wait_bar<T::RSUM>(sempty_bar(i), ph ^ 1u, abort_flag, tmo, kStatusTimeoutProducer))
             return false;
         ptx::st_shared_u32(ring + 4u * i, static_cast<uint32_t>(t));
         ptx::st_shared_cluster_u32(ptx::mapa(ring + 4u * i, 1), static_cast<uint32_t>(t));
@@ -385,7 +410,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
     auto ring_take = [&](int &t, unsigned code, unsigned backoff_ns) -> bool {
         const int i = ring_seq % kSchedDepth;
         const uint32_t ph = static_cast<uint32_t>(ring_seq / kSchedDepth) & 1u;
-        if (!wait_bar(sfull_bar(i), ph, abort_flag, tmo, code, backoff_ns))
+        if (!wait_bar<T::RSUM>(sfull_bar(i), ph, abort_flag, tmo, code, backoff_ns))
             return false;
         t = static_cast<int>(ptx::ld_shared_u32(ring + 4u * i));
         ring_release(i);
@@ -393,263 +418,276 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
         return true;
     };
 
-    if (warp == 0) {
-        // ───────────────────────── TMA producer ─────────────────────────
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int issued = 0;
-            bool ok = true;
-            UnitIter it;
-            it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
-                    args.num_kb, args.splits);
-            WorkUnit u;
-            auto next_unit = [&]() -> bool {
-                if constexpr (DYN) {
-                    int t = total_tiles;
-                    ok = (rank == 0) ? ring_post(t) : ring_take(t, kStatusTimeoutProducer, 0);
-                    if (!ok || t >= total_tiles)
-                        return false;
-                    dyn_fill(t, u);
-                    return true;
-                } else {
-                    return it.next(u);
-                }
-            };
-            while (ok && next_unit()) {
-                const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
-                const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
-                for (int kb = u.kb0; kb < u.kb1; ++kb) {
-                    if (!wait_bar(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
-                                  kStatusTimeoutProducer)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t fb = full_bar(stage);
-                    if constexpr (CG == 1) {
-                        ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
-                        ptx::tma_load_2d(sA + stage * T::A_BYTES, &mapA, fb, kb * T::BK, a_row);
-                        ptx::tma_load_2d(sB + stage * T::B_BYTES, &mapB, fb, kb * T::BK, b_row);
+    if (warp < T::EPI_WARP0) {
+        // Warpgroup 0 of the RSUM kernels (producer, MMA issuer, two idle warps) needs few
+        // registers; the epilogue warpgroups hold the running sums. Each warpgroup executes
+        // its setmaxnreg together, at the head of its branch.
+        if constexpr (T::RSUM)
+            ptx::setmaxnreg_dec<T::RSUM_REGS_LOW>();
+        if (warp == 0) {
+            // ───────────────────────── TMA producer ─────────────────────────
+            if (lane == 0) {
+                int stage = 0;
+                uint32_t phase = 0;
+                int issued = 0;
+                bool ok = true;
+                UnitIter it;
+                it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                        args.num_kb, args.splits);
+                WorkUnit u;
+                auto next_unit = [&]() -> bool {
+                    if constexpr (DYN) {
+                        int t = total_tiles;
+                        ok = (rank == 0) ? ring_post(t) : ring_take(t, kStatusTimeoutProducer, 0);
+                        if (!ok || t >= total_tiles)
+                            return false;
+                        dyn_fill(t, u);
+                        return true;
                     } else {
-                        if (rank == 0)
-                            ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
-                        const uint32_t leader_fb = ptx::mapa(fb, 0);
-                        ptx::tma_load_2d_pair(sA + stage * T::A_BYTES, &mapA, leader_fb,
-                                              kb * T::BK, a_row);
-                        ptx::tma_load_2d_pair(sB + stage * T::B_BYTES, &mapB, leader_fb,
-                                              kb * T::BK, b_row);
+                        return it.next(u);
                     }
-                    ++issued;
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
+                };
+                while (ok && next_unit()) {
+                    const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
+                    const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
+                    for (int kb = u.kb0; kb < u.kb1; ++kb) {
+                        if (!wait_bar<T::RSUM>(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
+                                      kStatusTimeoutProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = full_bar(stage);
+                        if constexpr (CG == 1) {
+                            ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
+                            ptx::tma_load_2d(sA + stage * T::A_BYTES, &mapA, fb, kb * T::BK, a_row);
+                            ptx::tma_load_2d(sB + stage * T::B_BYTES, &mapB, fb, kb * T::BK, b_row);
+                        } else {
+                            if (rank == 0)
+                                ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
+                            const uint32_t leader_fb = ptx::mapa(fb, 0);
+                            ptx::tma_load_2d_pair(sA + stage * T::A_BYTES, &mapA, leader_fb,
+                                                  kb * T::BK, a_row);
+                            ptx::tma_load_2d_pair(sB + stage * T::B_BYTES, &mapB, leader_fb,
+                                                  kb * T::BK, b_row);
+                        }
+                        ++issued;
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                     }
                 }
-            }
-            // Drain: the most recent phase issued on each stage must have landed before
-            // this CTA may exit (already true on the normal path; bounded otherwise).
-            if ((CG == 1 || rank == 0) && !ok) {
-                const int n = issued < STAGES ? issued : STAGES;
-                for (int i = 0; i < n; ++i) {
-                    int s = stage - 1 - i;
-                    uint32_t ph = phase;
-                    if (s < 0) {
-                        s += STAGES;
-                        ph ^= 1u;
-                    }
-                    if (!ptx::mbar_try_wait(full_bar(s), ph)) {
-                        const uint64_t t0 = ptx::global_timer_ns();
-                        while (!ptx::mbar_try_wait(full_bar(s), ph) &&
-                               ptx::global_timer_ns() - t0 < tmo) {
+                // Drain: the most recent phase issued on each stage must have landed before
+                // this CTA may exit (already true on the normal path; bounded otherwise).
+                if ((CG == 1 || rank == 0) && !ok) {
+                    const int n = issued < STAGES ? issued : STAGES;
+                    for (int i = 0; i < n; ++i) {
+                        int s = stage - 1 - i;
+                        uint32_t ph = phase;
+                        if (s < 0) {
+                            s += STAGES;
+                            ph ^= 1u;
+                        }
+                        if (!ptx::mbar_try_wait(full_bar(s), ph)) {
+                            const uint64_t t0 = ptx::global_timer_ns();
+                            while (!ptx::mbar_try_wait(full_bar(s), ph) &&
+                                   ptx::global_timer_ns() - t0 < tmo) {
+                            }
                         }
                     }
                 }
             }
-        }
-    } else if (warp == 1) {
-        // ───────────────────────── MMA issuer ─────────────────────────
-        if (rank == 0 && lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
-            bool ok = true;
-            bool any = false;
-            auto advance = [&]() {
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            };
-            // MMAs of one k-block for accumulator half `h` (columns [256h, 256h+256)).
-            auto issue = [&](uint32_t d, int h, int kb) {
-                const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
-                const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES + h * T::B_SUB_BYTES);
+        } else if (warp == 1) {
+            // ───────────────────────── MMA issuer ─────────────────────────
+            if (rank == 0 && lane == 0) {
+                int stage = 0;
+                uint32_t phase = 0;
+                int acc = 0;
+                uint32_t acc_phase = 0;
+                bool ok = true;
+                bool any = false;
+                auto advance = [&]() {
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                };
+                // MMAs of one k-block for accumulator half `h` (columns [256h, 256h+256)). `kb` counts
+                // the k-blocks of the accumulation run: at 0 the first MMA overwrites D.
+                auto issue = [&](uint32_t d, int h, int kb) {
+                    const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
+                    const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES + h * T::B_SUB_BYTES);
 #pragma unroll
-                for (int k = 0; k < T::BK / 16; ++k) {
-                    // +32 B per 16-element K step = +2 in the start-address field.
-                    ptx::mma_f16<CG>(d + 256u * h, a0 + 2u * k, b0 + 2u * k, T::IDESC,
-                                     (kb | k) != 0 ? 1u : 0u);
-                }
-            };
-            auto commit_to = [&](uint32_t bar) {
-                if constexpr (CG == 1)
-                    ptx::mma_commit(bar);
-                else
-                    ptx::mma_commit_pair(bar, 0x3);
-            };
-            UnitIter it;
-            it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
-                    args.num_kb, args.splits);
-            WorkUnit u;
-            auto next_unit = [&]() -> bool {
-                if constexpr (DYN) {
-                    int t = total_tiles;
-                    ok = ring_take(t, kStatusTimeoutMma, 0);
-                    if (!ok || t >= total_tiles)
-                        return false;
-                    dyn_fill(t, u);
-                    return true;
-                } else {
-                    return it.next(u);
-                }
-            };
-            while (ok && next_unit()) {
-                const int nkb = u.kb1 - u.kb0; // k-blocks of this unit; MMAs index them from 0
-                if constexpr (PROMOTE && T::ACC_BUFS == 2) {
-                    for (int c0 = 0; c0 < nkb && ok; c0 += args.promote_kb) {
-                        const int c1 = min(nkb, c0 + args.promote_kb);
-                        if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo,
+                    for (int k = 0; k < T::BK / 16; ++k) {
+                        // +32 B per 16-element K step = +2 in the start-address field.
+                        ptx::mma_f16<CG>(d + 256u * h, a0 + 2u * k, b0 + 2u * k, T::IDESC,
+                                         (kb | k) != 0 ? 1u : 0u);
+                    }
+                };
+                auto commit_to = [&](uint32_t bar) {
+                    if constexpr (CG == 1)
+                        ptx::mma_commit(bar);
+                    else
+                        ptx::mma_commit_pair(bar, 0x3);
+                };
+                UnitIter it;
+                it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                        args.num_kb, args.splits);
+                WorkUnit u;
+                auto next_unit = [&]() -> bool {
+                    if constexpr (DYN) {
+                        int t = total_tiles;
+                        ok = ring_take(t, kStatusTimeoutMma, 0);
+                        if (!ok || t >= total_tiles)
+                            return false;
+                        dyn_fill(t, u);
+                        return true;
+                    } else {
+                        return it.next(u);
+                    }
+                };
+                while (ok && next_unit()) {
+                    const int nkb = u.kb1 - u.kb0; // k-blocks of this unit; MMAs index them from 0
+                    if constexpr (PROMOTE && T::ACC_BUFS == 2) {
+                        for (int c0 = 0; c0 < nkb && ok; c0 += args.promote_kb) {
+                            const int c1 = min(nkb, c0 + args.promote_kb);
+                            if (!wait_bar<T::RSUM>(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo,
+                                          kStatusTimeoutMma)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                            for (int kb = c0; kb < c1; ++kb) {
+                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                                ptx::tc_fence_after();
+                                issue(tmem_base, 0, kb - c0); // a fresh chain at each chunk start
+                                any = true;
+                                commit_to(empty_bar(stage));
+                                advance();
+                            }
+                            if (!ok)
+                                break;
+                            commit_to(tfull_bar(0));
+                            acc_phase ^= 1u;
+                        }
+                        if (!ok)
+                            break;
+                    } else if constexpr (T::ACC_BUFS == 2) {
+                        if (!wait_bar<T::RSUM>(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
                                       kStatusTimeoutMma)) {
                             ok = false;
                             break;
                         }
                         ptx::tc_fence_after();
-                        for (int kb = c0; kb < c1; ++kb) {
-                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::ACC_STRIDE);
+                        for (int kb = 0; kb < nkb; ++kb) {
+                            if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                                 ok = false;
                                 break;
                             }
                             ptx::tc_fence_after();
-                            issue(tmem_base, 0, kb - c0); // a fresh chain at each chunk start
+                            issue(d, 0, kb);
                             any = true;
                             commit_to(empty_bar(stage));
                             advance();
                         }
                         if (!ok)
                             break;
-                        commit_to(tfull_bar(0));
-                        acc_phase ^= 1u;
-                    }
-                    if (!ok)
-                        break;
-                } else if constexpr (T::ACC_BUFS == 2) {
-                    if (!wait_bar(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
-                                  kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    ptx::tc_fence_after();
-                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::ACC_STRIDE);
-                    for (int kb = 0; kb < nkb; ++kb) {
-                        if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
-                            ok = false;
-                            break;
-                        }
-                        ptx::tc_fence_after();
-                        issue(d, 0, kb);
-                        any = true;
-                        commit_to(empty_bar(stage));
-                        advance();
-                    }
-                    if (!ok)
-                        break;
-                    commit_to(tfull_bar(acc));
-                    acc ^= 1;
-                    if (acc == 0)
-                        acc_phase ^= 1u;
-                } else {
-                    // One accumulator (both halves of TMEM). PROMOTE cuts the tile's K range
-                    // into chunks, each accumulated from zero; otherwise one chunk = the tile.
-                    // Per chunk, half 0 runs ahead over the first `run` k-blocks while the
-                    // epilogue still drains half 1 of the previous chunk or tile.
-                    const int chunk = PROMOTE ? args.promote_kb : nkb;
-                    for (int c0 = 0; c0 < nkb && ok; c0 += chunk) {
-                        const int n = (nkb - c0) < chunk ? (nkb - c0) : chunk;
-                        if (!wait_bar(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
-                            ok = false;
-                            break;
-                        }
-                        ptx::tc_fence_after();
-                        const int run = n < STAGES ? n : STAGES;
-                        const int s0 = stage;
-                        const uint32_t p0 = phase;
-                        for (int kb = 0; kb < run; ++kb) {
-                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                        commit_to(tfull_bar(acc));
+                        acc ^= 1;
+                        if (acc == 0)
+                            acc_phase ^= 1u;
+                    } else {
+                        // One accumulator (both halves of TMEM). PROMOTE cuts the tile's K range
+                        // into chunks; otherwise one chunk = the tile. The first chunk starts from
+                        // zero, every later one from the value the epilogue left in TMEM (the
+                        // rounding remainder of its register-held running sum). Per chunk, half 0
+                        // runs ahead over the first `run` k-blocks while the epilogue still drains
+                        // half 1 of the previous chunk or tile.
+                        const int chunk = PROMOTE ? args.promote_kb : nkb;
+                        for (int c0 = 0; c0 < nkb && ok; c0 += chunk) {
+                            const int n = (nkb - c0) < chunk ? (nkb - c0) : chunk;
+                            const int kb_base = (PROMOTE && c0 > 0) ? 1 : 0; // carry: accumulate
+                            if (!wait_bar<T::RSUM>(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
                                 ok = false;
                                 break;
                             }
                             ptx::tc_fence_after();
-                            issue(tmem_base, 0, kb);
-                            any = true;
-                            advance();
-                        }
-                        if (!ok)
-                            break;
-                        if (!wait_bar(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
-                            ok = false;
-                            break;
-                        }
-                        ptx::tc_fence_after();
-                        stage = s0;
-                        phase = p0;
-                        for (int kb = 0; kb < run; ++kb) {
-                            issue(tmem_base, 1, kb);
-                            commit_to(empty_bar(stage));
-                            advance();
-                        }
-                        for (int kb = run; kb < n; ++kb) {
-                            if (!wait_bar(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                            const int run = n < STAGES ? n : STAGES;
+                            const int s0 = stage;
+                            const uint32_t p0 = phase;
+                            for (int kb = 0; kb < run; ++kb) {
+                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                                ptx::tc_fence_after();
+                                issue(tmem_base, 0, kb_base + kb);
+                                any = true;
+                                advance();
+                            }
+                            if (!ok)
+                                break;
+                            if (!wait_bar<T::RSUM>(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
                                 ok = false;
                                 break;
                             }
                             ptx::tc_fence_after();
-                            issue(tmem_base, 0, kb);
-                            issue(tmem_base, 1, kb);
-                            commit_to(empty_bar(stage));
-                            advance();
+                            stage = s0;
+                            phase = p0;
+                            for (int kb = 0; kb < run; ++kb) {
+                                issue(tmem_base, 1, kb_base + kb);
+                                commit_to(empty_bar(stage));
+                                advance();
+                            }
+                            for (int kb = run; kb < n; ++kb) {
+                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                                ptx::tc_fence_after();
+                                issue(tmem_base, 0, kb_base + kb);
+                                issue(tmem_base, 1, kb_base + kb);
+                                commit_to(empty_bar(stage));
+                                advance();
+                            }
+                            if (!ok)
+                                break;
+                            commit_to(tfull_bar(0));
+                            acc_phase ^= 1u;
                         }
                         if (!ok)
                             break;
-                        commit_to(tfull_bar(0));
-                        acc_phase ^= 1u;
                     }
-                    if (!ok)
-                        break;
                 }
-            }
-            // Every MMA issued by this thread must complete before TMEM is freed.
-            if (any) {
-                if constexpr (CG == 1)
-                    ptx::mma_commit(drain_bar);
-                else
-                    ptx::mma_commit_pair(drain_bar, 0x1);
-                if (!ptx::mbar_try_wait(drain_bar, 0)) {
-                    const uint64_t t0 = ptx::global_timer_ns();
-                    while (!ptx::mbar_try_wait(drain_bar, 0)) {
-                        if (ptx::global_timer_ns() - t0 > tmo) {
-                            atomicCAS(&vg_status_word, 0u, (unsigned)kStatusTimeoutDrain);
-                            break;
+                // Every MMA issued by this thread must complete before TMEM is freed.
+                if (any) {
+                    if constexpr (CG == 1)
+                        ptx::mma_commit(drain_bar);
+                    else
+                        ptx::mma_commit_pair(drain_bar, 0x1);
+                    if (!ptx::mbar_try_wait(drain_bar, 0)) {
+                        const uint64_t t0 = ptx::global_timer_ns();
+                        while (!ptx::mbar_try_wait(drain_bar, 0)) {
+                            if (ptx::global_timer_ns() - t0 > tmo) {
+                                atomicCAS(&vg_status_word, 0u, (unsigned)kStatusTimeoutDrain);
+                                break;
+                            }
                         }
                     }
                 }
             }
         }
     } else {
+        if constexpr (T::RSUM)
+            ptx::setmaxnreg_inc<T::RSUM_REGS_HIGH>();
         // ───────────────────────── epilogue ─────────────────────────
-        const int sub = warp & 3;    // TMEM sub-partition this warp may read
-        const int ew = warp - 2;     // staging-buffer owner index
-        const int group = ew >> 2;   // which chunks of the tile this warp handles
+        const int sub = warp & 3;           // TMEM sub-partition this warp may read
+        const int ew = warp - T::EPI_WARP0; // staging-buffer owner index
+        const int group = ew >> 2;          // which chunks of the tile this warp handles
         int acc = 0;
         uint32_t acc_phase = 0;
         int buf = 0;
@@ -683,190 +721,258 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                 return it.next(u);
             }
         };
-        // PROMOTE with one accumulator: this CTA's running-sum slot, column-quad major
-        // ([BN/4 quads][128 rows][4 floats]: a warp's 32 rows of one quad are 512
-        // contiguous bytes).
-        float *const pslot = (PROMOTE && T::ACC_BUFS == 1 && args.promote_slots)
-                                 ? args.promote_slots + static_cast<long long>(blockIdx.x) * (T::BM * T::BN)
-                                 : nullptr;
-        const long long prow = (static_cast<long long>(sub) * 32 + lane) * 4;
-        // The slot's lines stay in L2 ahead of the streaming A/B tiles (evict_last): with the
-        // default policy nearly every add missed L2 and went to DRAM and back (measured: 93 %
-        // of the reduction sectors missed at 8192x8192x32768, +1.8 GB read and written).
-        const uint64_t slot_pol = (PROMOTE && T::ACC_BUFS == 1) ? ptx::l2_policy_evict_last() : 0;
         while (epi_ok && next_unit()) {
           // PROMOTE: one pass per K chunk; only the last one stores C.
           const int nkc = PROMOTE ? (u.kb1 - u.kb0 + args.promote_kb - 1) / args.promote_kb : 1;
+          const int row0 = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
+          const int col0 = u.tile_n * T::BN;
+          const int cend = min(args.N, col0 + T::BN); // columns of this tile that exist
+          const uint32_t t_row =
+              tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
+          // Stores one 64-column chunk (accumulator chunk c, 32 rows per warp) of C in the
+          // epilogue's output form.
+          auto emit = [&](int c, uint32_t (&v0)[32], uint32_t (&v1)[32]) {
+              const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
+              if constexpr (EPI == kEpiStagedF16) {
+                  // C rows are not 16-B aligned (N % 8 != 0 or an offset base): stage the
+                  // 32 × 64 box, then write it row by row, 32 lanes covering 64 contiguous
+                  // bytes per store instruction.
+                  uint32_t p[32];
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                      p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
+                      p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
+                  }
+                  const uint32_t stg = sEpi + static_cast<uint32_t>(ew * L::EPI_BUFS * T::STG_BYTES);
+                  __syncwarp(); // previous chunk's reads of this buffer are done
+                  const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                      const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
+                      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                                   "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
+                                   "r"(p[4 * j + 3])
+                                   : "memory");
+                  }
+                  __syncwarp();
+                  __half *cbase = static_cast<__half *>(args.C);
+#pragma unroll 4
+                  for (int r = 0; r < 32; ++r) {
+                      const int grow = row0 + r;
+                      if (grow >= args.M)
+                          break;
+                      __half *crow = cbase + static_cast<long long>(grow) * args.ldc;
+#pragma unroll
+                      for (int h = 0; h < 2; ++h) {
+                          const int col = h * 32 + lane; // column within the box
+                          const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
+                                             (static_cast<uint32_t>((col >> 3) ^ (r & 7)) << 4) +
+                                             static_cast<uint32_t>(col & 7) * 2u;
+                          unsigned short bits;
+                          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(a));
+                          if (ccol + col < cend)
+                              reinterpret_cast<unsigned short *>(crow)[ccol + col] = bits;
+                      }
+                  }
+              } else if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
+                  uint32_t p[32];
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) {
+                      p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
+                      p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
+                  }
+                  const uint32_t stg = sEpi + static_cast<uint32_t>((ew * L::EPI_BUFS + buf) * T::STG_BYTES);
+                  if (lane == 0)
+                      ptx::bulk_wait_group_read<L::EPI_BUFS - 1>();
+                  __syncwarp();
+                  const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                      const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
+                      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                                   "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
+                                   "r"(p[4 * j + 3])
+                                   : "memory");
+                  }
+                  ptx::fence_proxy_async_smem();
+                  __syncwarp();
+                  if (lane == 0) {
+                      if (row0 < args.M && ccol < args.N)
+                          ptx::tma_store_2d(&mapC, stg, ccol, row0);
+                      ptx::bulk_commit_group();
+                  }
+                  if constexpr (EPI == kEpiTmaF16Peers) {
+                      // Fused all-gather: the staged 32 × 64 box goes to every peer's C
+                      // over NVLink, eight lanes per row so that each row leaves as one
+                      // contiguous 128-B write (reads undo the 128-B swizzle).
+                      const int sub_row = lane >> 3, j = lane & 7;
+#pragma unroll
+                      for (int i = 0; i < 8; ++i) {
+                          const int r = i * 4 + sub_row;
+                          const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
+                                             (static_cast<uint32_t>(j ^ (r & 7)) << 4);
+                          uint4 q;
+                          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                       : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
+                                       : "r"(a));
+                          const int grow = row0 + r;
+                          const int gcol = ccol + 8 * j;
+                          if (grow < args.M && gcol < cend) {
+                              const long long off = static_cast<long long>(grow) * args.ldc + gcol;
+                              if (args.mc) {
+                                  const __half *dst = static_cast<__half *>(args.mc) + off;
+                                  asm volatile("multimem.st.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                                               "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w)
+                                               : "memory");
+                              } else {
+                                  for (int pr = 0; pr < args.num_peers; ++pr)
+                                      *reinterpret_cast<uint4 *>(static_cast<__half *>(args.peers[pr]) + off) = q;
+                              }
+                          }
+                      }
+                  }
+                  buf = (buf + 1) % L::EPI_BUFS;
+              } else if constexpr (EPI == kEpiDirectF16) {
+                  const int row = row0 + lane;
+                  if (row < args.M) {
+                      __half *crow = static_cast<__half *>(args.C) + static_cast<long long>(row) * args.ldc;
+#pragma unroll
+                      for (int j = 0; j < 8; ++j) {
+                          const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
+                          const int col = ccol + 8 * j;
+                          if (args.c_vec_ok && col + 8 <= cend) {
+                              uint4 q;
+                              q.x = pack_half2(v[0], v[1]);
+                              q.y = pack_half2(v[2], v[3]);
+                              q.z = pack_half2(v[4], v[5]);
+                              q.w = pack_half2(v[6], v[7]);
+                              *reinterpret_cast<uint4 *>(crow + col) = q;
+                          } else {
+#pragma unroll
+                              for (int e = 0; e < 8; ++e)
+                                  if (col + e < cend)
+                                      crow[col + e] = __float2half_rn(__uint_as_float(v[e]));
+                          }
+                      }
+                  }
+              } else {
+                  const int row = row0 + lane;
+                  if (row < args.M) {
+                      float *crow = static_cast<float *>(args.C) + u.split * args.split_stride +
+                                    static_cast<long long>(row) * args.ldc;
+#pragma unroll
+                      for (int j = 0; j < 8; ++j) {
+                          const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
+                          const int col = ccol + 8 * j;
+                          if (args.c_vec_ok && col + 8 <= cend) {
+                              float4 q0 = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]),
+                                                      __uint_as_float(v[2]), __uint_as_float(v[3]));
+                              float4 q1 = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]),
+                                                      __uint_as_float(v[6]), __uint_as_float(v[7]));
+                              *reinterpret_cast<float4 *>(crow + col) = q0;
+                              *reinterpret_cast<float4 *>(crow + col + 4) = q1;
+                          } else {
+#pragma unroll
+                              for (int e = 0; e < 8; ++e)
+                                  if (col + e < cend)
+                                      crow[col + e] = __uint_as_float(v[e]);
+                          }
+                      }
+                  }
+              }
+          };
+          if constexpr (T::RSUM) {
+            if (nkc > 1) {
+              // This thread's running sums over the tile's chunks, as bf16 pairs (one row,
+              // the warp's 256 columns: [half][chunk of the half][32-column piece][pair]).
+              // Each chunk boundary rounds sum + chunk to bf16 here and leaves the exact
+              // remainder in TMEM, where the next chunk's MMAs accumulate on top of it.
+              constexpr int RS_CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS;
+              uint32_t rsum[T::NSUB][RS_CPH][2][16];
+              auto add_sum = [](uint32_t &x0, uint32_t &x1, uint32_t pair) {
+                  x0 = __float_as_uint(__uint_as_float(x0) + ptx::bf16_lo(pair));
+                  x1 = __float_as_uint(__uint_as_float(x1) + ptx::bf16_hi(pair));
+              };
+              auto release_half = [&](int h) {
+                  ptx::tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0)
+                      ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
+              };
+              for (int j = 0; j < nkc && epi_ok; ++j) {
+                if (!wait_bar<T::RSUM>(tfull_bar(0), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
+                              VG_EPI_BACKOFF_NS)) {
+                    epi_ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                // Per half: for each of this warp's 32-column pieces, s = sum + chunk (the
+                // chunk accumulated on top of the previous remainder); not the last chunk:
+                // sum = bf16(s) and TMEM = s - sum, then the half back to the MMA issuer;
+                // the last chunk: the half back once loaded, C = s.
+                const bool last = (j + 1 == nkc);
+#pragma unroll
+                for (int h = 0; h < T::NSUB; ++h) {
+#pragma unroll
+                    for (int i = 0; i < RS_CPH; ++i) {
+                        const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
+                        if (!last) {
+#pragma unroll
+                            for (int p = 0; p < 2; ++p) {
+                                uint32_t v[32];
+                                ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32 * p, v);
+                                ptx::tmem_wait_ld();
+#pragma unroll
+                                for (int e = 0; e < 16; ++e) {
+                                    if (j > 0)
+                                        add_sum(v[2 * e], v[2 * e + 1], rsum[h][i][p][e]);
+                                    const float s0 = __uint_as_float(v[2 * e]);
+                                    const float s1 = __uint_as_float(v[2 * e + 1]);
+                                    const uint32_t r = ptx::pack_bf16x2_rn(s0, s1);
+                                    rsum[h][i][p][e] = r;
+                                    v[2 * e] = __float_as_uint(s0 - ptx::bf16_lo(r));
+                                    v[2 * e + 1] = __float_as_uint(s1 - ptx::bf16_hi(r));
+                                }
+                                ptx::tmem_st_32x32b_x32(t_row + c * 64 + 32 * p, v);
+                            }
+                        } else {
+                            uint32_t v0[32], v1[32];
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
+                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
+                            ptx::tmem_wait_ld();
+                            if (i == RS_CPH - 1)
+                                release_half(h);
+#pragma unroll
+                            for (int e = 0; e < 16; ++e) {
+                                add_sum(v0[2 * e], v0[2 * e + 1], rsum[h][i][0][e]);
+                                add_sum(v1[2 * e], v1[2 * e + 1], rsum[h][i][1][e]);
+                            }
+                            emit(c, v0, v1);
+                        }
+                    }
+                    if (!last) {
+                        ptx::tmem_wait_st(); // the remainders are in TMEM before the hand-back
+                        release_half(h);
+                    }
+                }
+                acc_phase ^= 1u; // every chunk lands in the one accumulator
+              }
+              continue;
+            }
+          }
           for (int j = 0; j < nkc && epi_ok; ++j) {
-            if (!wait_bar(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
+            if (!wait_bar<T::RSUM>(tfull_bar(acc), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
                           VG_EPI_BACKOFF_NS)) {
                 epi_ok = false;
                 break;
             }
             ptx::tc_fence_after();
-            const int row0 = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM + sub * 32;
-            const int col0 = u.tile_n * T::BN;
-            const int cend = min(args.N, col0 + T::BN); // columns of this tile that exist
             // Owner of a split tile: the contributors' partials must have landed.
             if (SK && u.kind == kUnitOwner) {
                 for (int c = u.first_contrib; c <= u.last_contrib && epi_ok; ++c)
                     epi_ok = wait_flag(args.sk_flags + c * CG + rank, abort_flag, tmo);
                 __syncwarp();
             }
-            const uint32_t t_row =
-                tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * T::ACC_STRIDE);
-            // Stores one 64-column chunk (accumulator chunk c, 32 rows per warp) of C in the
-            // epilogue's output form.
-            auto emit = [&](int c, uint32_t (&v0)[32], uint32_t (&v1)[32]) {
-                const int ccol = col0 + acc_col_to_c<T::NSUB>(c * 64);
-                if constexpr (EPI == kEpiStagedF16) {
-                    // C rows are not 16-B aligned (N % 8 != 0 or an offset base): stage the
-                    // 32 × 64 box, then write it row by row, 32 lanes covering 64 contiguous
-                    // bytes per store instruction.
-                    uint32_t p[32];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
-                        p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
-                    }
-                    const uint32_t stg = sEpi + static_cast<uint32_t>(ew * L::EPI_BUFS * T::STG_BYTES);
-                    __syncwarp(); // previous chunk's reads of this buffer are done
-                    const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
-                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                                     "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
-                                     "r"(p[4 * j + 3])
-                                     : "memory");
-                    }
-                    __syncwarp();
-                    __half *cbase = static_cast<__half *>(args.C);
-#pragma unroll 4
-                    for (int r = 0; r < 32; ++r) {
-                        const int grow = row0 + r;
-                        if (grow >= args.M)
-                            break;
-                        __half *crow = cbase + static_cast<long long>(grow) * args.ldc;
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int col = h * 32 + lane; // column within the box
-                            const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
-                                               (static_cast<uint32_t>((col >> 3) ^ (r & 7)) << 4) +
-                                               static_cast<uint32_t>(col & 7) * 2u;
-                            unsigned short bits;
-                            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(bits) : "r"(a));
-                            if (ccol + col < cend)
-                                reinterpret_cast<unsigned short *>(crow)[ccol + col] = bits;
-                        }
-                    }
-                } else if constexpr (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers) {
-                    uint32_t p[32];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        p[i] = pack_half2(v0[2 * i], v0[2 * i + 1]);
-                        p[16 + i] = pack_half2(v1[2 * i], v1[2 * i + 1]);
-                    }
-                    const uint32_t stg = sEpi + static_cast<uint32_t>((ew * L::EPI_BUFS + buf) * T::STG_BYTES);
-                    if (lane == 0)
-                        ptx::bulk_wait_group_read<L::EPI_BUFS - 1>();
-                    __syncwarp();
-                    const uint32_t row_addr = stg + static_cast<uint32_t>(lane) * 128u;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t a = row_addr + (static_cast<uint32_t>(j ^ (lane & 7)) << 4);
-                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                                     "r"(p[4 * j]), "r"(p[4 * j + 1]), "r"(p[4 * j + 2]),
-                                     "r"(p[4 * j + 3])
-                                     : "memory");
-                    }
-                    ptx::fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (row0 < args.M && ccol < args.N)
-                            ptx::tma_store_2d(&mapC, stg, ccol, row0);
-                        ptx::bulk_commit_group();
-                    }
-                    if constexpr (EPI == kEpiTmaF16Peers) {
-                        // Fused all-gather: the staged 32 × 64 box goes to every peer's C
-                        // over NVLink, eight lanes per row so that each row leaves as one
-                        // contiguous 128-B write (reads undo the 128-B swizzle).
-                        const int sub_row = lane >> 3, j = lane & 7;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int r = i * 4 + sub_row;
-                            const uint32_t a = stg + static_cast<uint32_t>(r) * 128u +
-                                               (static_cast<uint32_t>(j ^ (r & 7)) << 4);
-                            uint4 q;
-                            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                                         : "=r"(q.x), "=r"(q.y), "=r"(q.z), "=r"(q.w)
-                                         : "r"(a));
-                            const int grow = row0 + r;
-                            const int gcol = ccol + 8 * j;
-                            if (grow < args.M && gcol < cend) {
-                                const long long off = static_cast<long long>(grow) * args.ldc + gcol;
-                                if (args.mc) {
-                                    const __half *dst = static_cast<__half *>(args.mc) + off;
-                                    asm volatile("multimem.st.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-                                                 "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w)
-                                                 : "memory");
-                                } else {
-                                    for (int pr = 0; pr < args.num_peers; ++pr)
-                                        *reinterpret_cast<uint4 *>(static_cast<__half *>(args.peers[pr]) + off) = q;
-                                }
-                            }
-                        }
-                    }
-                    buf = (buf + 1) % L::EPI_BUFS;
-                } else if constexpr (EPI == kEpiDirectF16) {
-                    const int row = row0 + lane;
-                    if (row < args.M) {
-                        __half *crow = static_cast<__half *>(args.C) + static_cast<long long>(row) * args.ldc;
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
-                            const int col = ccol + 8 * j;
-                            if (args.c_vec_ok && col + 8 <= cend) {
-                                uint4 q;
-                                q.x = pack_half2(v[0], v[1]);
-                                q.y = pack_half2(v[2], v[3]);
-                                q.z = pack_half2(v[4], v[5]);
-                                q.w = pack_half2(v[6], v[7]);
-                                *reinterpret_cast<uint4 *>(crow + col) = q;
-                            } else {
-#pragma unroll
-                                for (int e = 0; e < 8; ++e)
-                                    if (col + e < cend)
-                                        crow[col + e] = __float2half_rn(__uint_as_float(v[e]));
-                            }
-                        }
-                    }
-                } else {
-                    const int row = row0 + lane;
-                    if (row < args.M) {
-                        float *crow = static_cast<float *>(args.C) + u.split * args.split_stride +
-                                      static_cast<long long>(row) * args.ldc;
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const uint32_t *v = (j < 4) ? (v0 + 8 * j) : (v1 + 8 * (j - 4));
-                            const int col = ccol + 8 * j;
-                            if (args.c_vec_ok && col + 8 <= cend) {
-                                float4 q0 = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]),
-                                                        __uint_as_float(v[2]), __uint_as_float(v[3]));
-                                float4 q1 = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]),
-                                                        __uint_as_float(v[6]), __uint_as_float(v[7]));
-                                *reinterpret_cast<float4 *>(crow + col) = q0;
-                                *reinterpret_cast<float4 *>(crow + col + 4) = q1;
-                            } else {
-#pragma unroll
-                                for (int e = 0; e < 8; ++e)
-                                    if (col + e < cend)
-                                        crow[col + e] = __uint_as_float(v[e]);
-                            }
-                        }
-                    }
-                }
-            };
             bool drained = false; // this chunk was handled by a PROMOTE path below
             if constexpr (PROMOTE && T::ACC_BUFS == 2) {
                 // The warp's chunks of buffer 0 into registers, buffer 0 back to the MMA issuer
@@ -913,96 +1019,6 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
                         emit(c, v[i][0], v[i][1]);
                 }
                 drained = true;
-            }
-            if constexpr (PROMOTE && T::ACC_BUFS == 1) {
-                if (j + 1 < nkc) {
-                    // Per half: this warp's chunks of the half into registers, the half back
-                    // to the MMA issuer, then slot = (j == 0 ? 0 : slot) + chunk values.
-                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS; // warp's chunks per half
-#pragma unroll 1
-                    for (int h = 0; h < T::NSUB; ++h) {
-                        uint32_t v[CPH][2][32];
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
-                        }
-                        ptx::tmem_wait_ld();
-                        ptx::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0)
-                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-#pragma unroll
-                            for (int p = 0; p < 2; ++p) {
-                                // First chunk: store; later chunks: add in L2 (red, fire and
-                                // forget: no read latency on the way to the next half).
-                                float *dst = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
-#pragma unroll
-                                for (int q = 0; q < 8; ++q) {
-                                    const float a0 = __uint_as_float(v[i][p][4 * q]);
-                                    const float a1 = __uint_as_float(v[i][p][4 * q + 1]);
-                                    const float a2 = __uint_as_float(v[i][p][4 * q + 2]);
-                                    const float a3 = __uint_as_float(v[i][p][4 * q + 3]);
-                                    if (j == 0)
-                                        ptx::st_global_v4_hint(dst + q * (T::BM * 4), a0, a1, a2, a3, slot_pol);
-                                    else
-                                        ptx::red_add_v4_hint(dst + q * (T::BM * 4), a0, a1, a2, a3, slot_pol);
-                                }
-                            }
-                        }
-                    }
-                    drained = true;
-                } else if (nkc > 1) {
-                    // Last chunk of a multi-chunk tile: the same per-half hand-back (the slot
-                    // reads do not hold TMEM), then running sum + chunk, stored as C.
-                    constexpr int CPH = T::CHUNKS_PER_UNIT / T::EPI_GROUPS;
-#pragma unroll 1
-                    for (int h = 0; h < T::NSUB; ++h) {
-                        uint32_t v[CPH][2][32];
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64, v[i][0]);
-                            ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v[i][1]);
-                        }
-                        ptx::tmem_wait_ld();
-                        ptx::tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0)
-                            ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(h), 0));
-#pragma unroll
-                        for (int i = 0; i < CPH; ++i) {
-                            const int c = h * T::CHUNKS_PER_UNIT + group + i * T::EPI_GROUPS;
-#pragma unroll
-                            for (int p = 0; p < 2; ++p) {
-                                const float *src = pslot + prow + static_cast<long long>(c * 16 + p * 8) * (T::BM * 4);
-#pragma unroll
-                                for (int q = 0; q < 8; ++q) {
-                                    const float4 o = ptx::ld_global_cg_v4_hint(src + q * (T::BM * 4), slot_pol);
-                                    v[i][p][4 * q] = __float_as_uint(o.x + __uint_as_float(v[i][p][4 * q]));
-                                    v[i][p][4 * q + 1] = __float_as_uint(o.y + __uint_as_float(v[i][p][4 * q + 1]));
-                                    v[i][p][4 * q + 2] = __float_as_uint(o.z + __uint_as_float(v[i][p][4 * q + 2]));
-                                    v[i][p][4 * q + 3] = __float_as_uint(o.w + __uint_as_float(v[i][p][4 * q + 3]));
-                                }
-                                // The running sum of these lines is used up: drop them from L2
-                                // (no write-back; the next tile's first chunk rewrites them). Each
-                                // quad's 32 rows are 512 contiguous bytes = 4 lines, one per 8 lanes.
-                                __syncwarp();
-                                if ((lane & 7) == 0) {
-#pragma unroll
-                                    for (int q = 0; q < 8; ++q)
-                                        ptx::discard_l2_line(src + q * (T::BM * 4));
-                                }
-                            }
-                            emit(c, v[i][0], v[i][1]);
-                        }
-                    }
-                    drained = true;
-                }
             }
 #pragma unroll 1
             for (int c = group; c < T::NCHUNK && !drained; c += T::EPI_GROUPS) {
@@ -1089,7 +1105,7 @@ __global__ void __launch_bounds__(TileCfg<CG, BN>::THREADS, 1)
             if (SK && u.kind == kUnitPartial) {
                 // All epilogue warps' partial stores, then one release of the ready flag.
                 asm volatile("bar.sync 1, %0;" ::"n"(32 * T::EPI_WARPS) : "memory");
-                if (warp == 2 && lane == 0) {
+                if (warp == T::EPI_WARP0 && lane == 0) {
                     __threadfence();
                     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(args.sk_flags + it.w * CG + rank),
                                  "r"(1u)

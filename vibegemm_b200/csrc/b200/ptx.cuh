@@ -64,40 +64,27 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
     return v;
 }
 
-// L2 cache policy that keeps lines resident ahead of normally cached data (evict_last).
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
+// Per-warpgroup register budgets (setmaxnreg; all four warps of a warpgroup execute the same
+// one). A kernel launched with R registers per thread may hand registers from one warpgroup to
+// another as long as the warpgroups' budgets add up to no more than R per thread: `dec` first
+// returns registers to the CTA's pool, `inc` waits until the pool holds enough.
+template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
+    static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: multiple of 8 in [24, 256]");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
+    static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: multiple of 8 in [24, 256]");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
-// 16-byte global accesses with an L2 cache policy (st, and ld cached in L2 only), and a
-// fire-and-forget element-wise fp32 add of four floats performed in L2 (red: each element
-// is added atomically, round to nearest). A thread that reds into an address and later reads
-// it with ld.global.cg sees its own adds (same address, program order, both at L2).
-__device__ __forceinline__ void st_global_v4_hint(float *p, float a, float b, float c, float d, uint64_t pol) {
-    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(a), "f"(b),
-                 "f"(c), "f"(d), "l"(pol)
-                 : "memory");
+// Two fp32 values rounded to nearest bf16 and packed (lo in bits 0-15, hi in 16-31), and back.
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
 }
-__device__ __forceinline__ void red_add_v4_hint(float *p, float a, float b, float c, float d, uint64_t pol) {
-    asm volatile("red.global.add.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(a),
-                 "f"(b), "f"(c), "f"(d), "l"(pol)
-                 : "memory");
-}
-__device__ __forceinline__ float4 ld_global_cg_v4_hint(const float *p, uint64_t pol) {
-    float4 v;
-    asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p), "l"(pol)
-                 : "memory");
-    return v;
-}
-// Drops the 128-byte L2 line at p (128-B aligned) without writing it back: its contents
-// become indeterminate. For scratch data that is dead.
-__device__ __forceinline__ void discard_l2_line(const void *p) {
-    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
-}
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
 // ── mbarrier ──────────────────────────────────────────────────────────────────
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

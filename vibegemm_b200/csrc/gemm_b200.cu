@@ -82,8 +82,10 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v5", 1, 192, 4, true, true, 8},
     {"VibeGEMM B200 v6", 2, 512, 4, false, true, 16},
     {"VibeGEMM B200 v7", 1, 192, 5, true, true, 8},
-    {"VibeGEMM B200 v8", 2, 256, 6, true, true, 8, false, true, true},
-    {"VibeGEMM B200 v9", 2, 512, 4, true, true, 16, false, true, true},
+    // Raster groups of the chunked kernels measured at 32768³, sustained (TFLOP/s): v8 group 4
+    // 1183 vs 8 1105; v9 group 8 1303–1307 vs 16 1272–1291 vs 4 1274.
+    {"VibeGEMM B200 v8", 2, 256, 6, true, true, 4, false, true, true},
+    {"VibeGEMM B200 v9", 2, 512, 4, true, true, 8, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
 };
@@ -126,13 +128,17 @@ int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     const long long t2 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 256);
     // From K = kPromoteMinK on every output's sum is split into chains of at most 4096 (one
     // tensor-core chain per output exceeds the 1e-2 bound from K ~ 10000 on, 3.6e-2 at
-    // 32768): v8, the 256×256 pair with its running sum in TMEM and run-time tile claims
-    // (sustained at 32768³: 1146 TFLOP/s, against 1078 for v9, whose 256×512 tile keeps the
-    // sums in global memory, and 1298 for one chain, v10), or, over a grid at most half
-    // full, stream-K v4.
+    // 32768). Over at least a wave of 256×256 tiles: v9, the 256×512 pair whose running sums
+    // live in the epilogue warps' registers (sustained at 32768³ 1207–1243 TFLOP/s, level
+    // with one chain, v10, at 1216–1222), or v8, the 256×256 pair with its sums in TMEM
+    // (1077 there, 1.12x slower per tile), whichever needs fewer tile-waves by that ratio.
+    // Over fewer tiles, split-K v11 or v8 (below).
     const bool split_chains = K >= kPromoteMinK;
-    if (split_chains && t2 >= pairs)
-        return 8;
+    if (split_chains && t2 >= pairs) {
+        const double e9 = (double)((t3 + pairs - 1) / pairs) * 512 / 1.12;
+        const double e8 = (double)((t2 + pairs - 1) / pairs) * 256;
+        return e9 <= e8 ? 9 : 8;
+    }
     // Full waves of pair tiles: 256×512 (v3, ~6 % more work per pair-cycle than 256×256 at
     // 8192³) against 256×256 (v2), each charged for its last partial wave. Within 1.5 % v3
     // wins: it moves a quarter less data, which the estimate does not credit (8191×8193×4099:
@@ -549,6 +555,7 @@ cudaError_t launch_splitk_reduce(const float *ws, int S, int M, int N, void *C, 
 
 // ── kernel launch ────────────────────────────────────────────────────────────
 template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> struct Inst {
+    using T = TileCfg<CG, BN, PROMOTE && BN == 512>;
     static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
     static std::atomic<unsigned long long> attr_ready; // bit per device
     static int max_clusters[kMaxDevices];
@@ -560,11 +567,21 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> 
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
+        if constexpr (T::RSUM) {
+            // The warpgroups' setmaxnreg budgets must fit in what the CTA is launched with, or
+            // the epilogue's setmaxnreg.inc would wait forever: refuse the kernel instead.
+            cudaFuncAttributes fa{};
+            e = cudaFuncGetAttributes(&fa, kern);
+            if (e != cudaSuccess)
+                return e;
+            if (T::RSUM_REGS_LOW + 2 * T::RSUM_REGS_HIGH > 3 * fa.numRegs)
+                return cudaErrorInvalidConfiguration;
+        }
         int clusters = 0;
         if (CG == 2) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(2 * 1024, 1, 1);
-            cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
+            cfg.blockDim = dim3(T::THREADS, 1, 1);
             cfg.dynamicSmemBytes = kSmem;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -587,7 +604,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> 
         auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid, 1, 1);
-        cfg.blockDim = dim3(TileCfg<CG, BN>::THREADS, 1, 1);
+        cfg.blockDim = dim3(T::THREADS, 1, 1);
         cfg.dynamicSmemBytes = kSmem;
         cfg.stream = s;
         cudaLaunchAttribute attr[2];
@@ -680,13 +697,11 @@ cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
 
 inline size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
 
-// Byte layout of a call's workspace: padded A, padded B, stream-K partials, running-sum
-// slots of the chunked pair-tile accumulation, then the words zeroed before every launch
-// (stream-K ready flags, the run-time tile counter).
+// Byte layout of a call's workspace: padded A, padded B, stream-K partials, split-K partials,
+// then the words zeroed before every launch (stream-K ready flags, the run-time tile counter).
 struct WsLayout {
-    size_t a_off = 0, b_off = 0, part_off = 0, slot_off = 0, split_off = 0, flag_off = 0, ctr_off = 0;
+    size_t a_off = 0, b_off = 0, part_off = 0, split_off = 0, flag_off = 0, ctr_off = 0;
     size_t flag_bytes = 0, total = 0;
-    bool promote_slots = false;
 };
 
 WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
@@ -695,21 +710,17 @@ WsLayout workspace_layout(const Plan &p, int M, int N, int grid) {
     const size_t b = p.pad_b ? round_up_256((size_t)N * p.Kp * sizeof(__half)) : 0;
     const size_t sk_slots = p.stream_k ? (size_t)grid : 0; // one per (worker, CTA rank)
     const size_t part = sk_slots * 128 * (size_t)p.bn * sizeof(float);
-    // One 128 × BN fp32 running sum per CTA when the pair tile's K range has several chunks.
-    w.promote_slots = p.promote && p.bn == 512 && p.promote_kb < p.num_kb;
-    const size_t slot = w.promote_slots ? (size_t)grid * 128 * (size_t)p.bn * sizeof(float) : 0;
     // Split-K: one fp32 M × N partial per split.
     const size_t split = p.splits > 1 ? round_up_256((size_t)p.splits * M * N * sizeof(float)) : 0;
     const size_t words = sk_slots + (p.dyn ? 1 : 0);
     w.a_off = 0;
     w.b_off = a;
     w.part_off = a + b;
-    w.slot_off = a + b + part;
-    w.split_off = a + b + part + slot;
-    w.flag_off = a + b + part + slot + split;
+    w.split_off = a + b + part;
+    w.flag_off = a + b + part + split;
     w.ctr_off = w.flag_off + sk_slots * sizeof(unsigned);
     w.flag_bytes = words ? round_up_256(words * sizeof(unsigned)) : 0;
-    w.total = a + b + part + slot + split + w.flag_bytes;
+    w.total = a + b + part + split + w.flag_bytes;
     return w;
 }
 
@@ -820,7 +831,6 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     void *owned = nullptr; // pool allocation to free after the launch
     float *sk_partials = nullptr;
     unsigned *sk_flags = nullptr;
-    float *promote_slots = nullptr;
     unsigned *sched_ctr = nullptr;
     float *split_ws = nullptr;
     if (wl.total) {
@@ -854,8 +864,6 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
             sk_partials = reinterpret_cast<float *>(base + wl.part_off);
             sk_flags = reinterpret_cast<unsigned *>(base + wl.flag_off);
         }
-        if (wl.promote_slots)
-            promote_slots = reinterpret_cast<float *>(base + wl.slot_off);
         if (p.splits > 1)
             split_ws = reinterpret_cast<float *>(base + wl.split_off);
         if (p.dyn)
@@ -897,7 +905,6 @@ int launch_gemm(int version, const void *A, const void *B, void *C, int M, int N
     args.sk_partials = sk_partials;
     args.sk_flags = sk_flags;
     args.promote_kb = p.promote_kb;
-    args.promote_slots = promote_slots;
     args.sched_ctr = sched_ctr;
     args.num_peers = num_peers;
     for (int i = 0; i < num_peers; ++i)
