@@ -198,6 +198,34 @@ def test_long_k_acceptance(vg, orc, shape):
     assert vg.device_status() == 0
 
 
+def test_register_sums_carry_the_rounding_remainder(vg):
+    """v9 keeps each output's running sum over K chunks as bf16 in registers and writes the
+    rounding remainder back into TMEM, where the next chunk accumulates on top of it. With the
+    remainder carried, v9 equals v8 (fp32 sums in TMEM) up to a few fp32 roundings; had it been
+    dropped, the two would differ by about 2^-9 of |C| (~0.1 here). Also: v9 repeats bit for
+    bit, and its fp16 output is exactly its fp32 output rounded to nearest (same tiles, same
+    chunks, whichever pair claims a tile)."""
+    import torch
+    M, N, K = 512, 1024, 16384  # 4 chunks of 4096 per tile
+    p = vg.plan(9, M, N, K, 256, 256, 256)
+    assert p["promote_kb"] * 4 == p["num_kb"], p
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    dB = torch.empty((N, K), dtype=torch.float16, device="cuda").uniform_(-1, 1, generator=g)
+    c9 = vg.gemm_f32out(dA, dB, version=9)
+    c9b = vg.gemm_f32out(dA, dB, version=9)
+    c8 = vg.gemm_f32out(dA, dB, version=8)
+    h9 = vg.gemm(dA, dB, version=9)
+    torch.cuda.synchronize()
+    assert torch.equal(c9, c9b)
+    scale = c8.abs().max().item()
+    assert scale > 50  # sums of 16384 products of U[-1,1]: |C| reaches well past 2^6
+    assert (c9 - c8).abs().max().item() <= 2e-3
+    assert torch.equal(h9, c9.half())
+    assert vg.device_status() == 0
+
+
 def test_32768_cubed_default_path_meets_the_tolerance(vg, orc):
     """The sharded config's full problem, M = N = K = 32768, through the default entry point
     (v9: run-time tiles, chunks of 4096 carried in registers), on rows sampled across the M range
