@@ -295,6 +295,10 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
     using T = TileCfg<CG, BN, PROMOTE && BN == 512>;
     using L = SmemLayout<CG, BN, STAGES, EPI>;
     static_assert(L::T::EPI_WARPS == T::EPI_WARPS, "shared-memory layout sized for these warps");
+    // Single-accumulator tiles of the static walk (v3, v6) end half by half (tfull(0), then
+    // tfull(1)). Measured at 8192³: +0.4–0.7 % (burst 1514–1520 vs 1509–1510 TFLOP/s, sustained
+    // 1307–1312 vs 1302–1306); with run-time claims at 32768³ (v10) it lost 1.5 % sustained.
+    constexpr bool kHalfEnds = T::ACC_BUFS == 1 && !PROMOTE && !DYN;
     static_assert(!PROMOTE || ((T::ACC_BUFS == 2 || CG == 2) && !SK),
                   "PROMOTE: two TMEM buffers or the pair tile, no stream-K");
     static_assert(!DYN || (CG == 2 && !SK), "DYN: CTA pairs, no stream-K");
@@ -606,7 +610,11 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         // zero, every later one from the value the epilogue left in TMEM (the
                         // rounding remainder of its register-held running sum). Per chunk, half 0
                         // runs ahead over the first `run` k-blocks while the epilogue still drains
-                        // half 1 of the previous chunk or tile.
+                        // half 1 of the previous chunk or tile. With kHalfEnds a tile also ends
+                        // half first: its last `tail` k-blocks issue half 0, signal it on
+                        // tfull(0), then issue half 1 and signal tfull(1), so the epilogue
+                        // drains half 0 while the tensor pipe works through half 1's tail, and
+                        // the next tile's half 0 can start as soon as that drain is done.
                         const int chunk = PROMOTE ? args.promote_kb : nkb;
                         for (int c0 = 0; c0 < nkb && ok; c0 += chunk) {
                             const int n = (nkb - c0) < chunk ? (nkb - c0) : chunk;
@@ -643,7 +651,8 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                                 commit_to(empty_bar(stage));
                                 advance();
                             }
-                            for (int kb = run; kb < n; ++kb) {
+                            const int tail = kHalfEnds ? min(n - run, STAGES / 2) : 0;
+                            for (int kb = run; kb < n - tail; ++kb) {
                                 if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                                     ok = false;
                                     break;
@@ -656,7 +665,33 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             }
                             if (!ok)
                                 break;
-                            commit_to(tfull_bar(0));
+                            if constexpr (kHalfEnds) {
+                                const int s1 = stage;
+                                const uint32_t p1 = phase;
+                                for (int kb = n - tail; kb < n; ++kb) {
+                                    if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo,
+                                                           kStatusTimeoutMma)) {
+                                        ok = false;
+                                        break;
+                                    }
+                                    ptx::tc_fence_after();
+                                    issue(tmem_base, 0, kb_base + kb);
+                                    advance();
+                                }
+                                if (!ok)
+                                    break;
+                                commit_to(tfull_bar(0));
+                                stage = s1;
+                                phase = p1;
+                                for (int kb = n - tail; kb < n; ++kb) {
+                                    issue(tmem_base, 1, kb_base + kb);
+                                    commit_to(empty_bar(stage));
+                                    advance();
+                                }
+                                commit_to(tfull_bar(1));
+                            } else {
+                                commit_to(tfull_bar(0));
+                            }
                             acc_phase ^= 1u;
                         }
                         if (!ok)
@@ -1022,6 +1057,17 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
             }
 #pragma unroll 1
             for (int c = group; c < T::NCHUNK && !drained; c += T::EPI_GROUPS) {
+                if constexpr (kHalfEnds) {
+                    // This warp's first chunk of half 1: wait for half 1's own completion.
+                    if (c >= T::CHUNKS_PER_UNIT && c - T::EPI_GROUPS < T::CHUNKS_PER_UNIT) {
+                        if (!wait_bar<T::RSUM>(tfull_bar(1), acc_phase, abort_flag, tmo,
+                                               kStatusTimeoutEpilogue, VG_EPI_BACKOFF_NS)) {
+                            epi_ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                    }
+                }
                 uint32_t v0[32], v1[32];
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64, v0);
                 ptx::tmem_ld_32x32b_x32(t_row + c * 64 + 32, v1);
