@@ -936,7 +936,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
               };
               for (int j = 0; j < nkc && epi_ok; ++j) {
                 if (!wait_bar<T::RSUM>(tfull_bar(0), acc_phase, abort_flag, tmo, kStatusTimeoutEpilogue,
-                              VG_EPI_BACKOFF_NS)) {
+                                       VG_EPI_BACKOFF_NS)) {
                     epi_ok = false;
                     break;
                 }
