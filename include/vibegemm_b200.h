@@ -182,8 +182,9 @@ void vg_raster_tile(int t, int num_m, int num_n, int group_m, int *tile_m, int *
 /* Work units persistent worker `worker` of `workers` processes (host copy of the device
  * schedule, for tests): data-parallel (stream_k = 0: whole tiles in grouped-raster order;
  * with splits > 1, split-K: tile × K-split units, unit u = tile u % T over the K range of
- * split u / T) or stream-K (stream_k = 1: an equal share of the (tile, k-block)
- * iterations). Writes up to max_units records of 8 ints {tile_m, tile_n, kb0, kb1, kind (0
+ * split u / T), stream-K (stream_k = 1: an equal share of the (tile, k-block)
+ * iterations) or contiguous runs (stream_k = 2, the A-resident kernel: tiles
+ * [w·T/P, (w+1)·T/P) in row-major order). Writes up to max_units records of 8 ints {tile_m, tile_n, kb0, kb1, kind (0
  * whole tile or split, 1 partial written to the workspace, 2 owner that adds the partials
  * of workers first..last), first_contrib, last_contrib, split} and returns the number of
  * units (-1 on bad input). Replaces the tile walk of Schedule::next
@@ -196,14 +197,15 @@ int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, i
  * `version` may be -1 (per-shape choice). `mode`: 0 = fp16 C (vg_b200_gemm_f16),
  * 1 = fp32 C (vg_b200_gemm_f16_f32out), 2 = fp16 C with the fused all-gather
  * (vg_b200_gemm_f16_allgather, whose per-shape choice excludes stream-K).
- * Fields of `out` (int[19]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct fp16,
+ * Fields of `out` (int[20]): cta_group, stages, epilogue kind (0 TMA fp16, 1 direct fp16,
  * 2 direct fp32, 3 TMA fp16 + peer stores, 4 staged fp16 with coalesced row stores for C
  * rows TMA cannot describe, 5 split-K: fp32 partials then a reduction kernel writing fp16
  * C), pad_a, pad_b, padded K, num_m_tiles, num_n_tiles, num_kb, group_m, grid (CTAs),
  * persistent, tile columns, resolved version, stream-K, promote (chunked accumulation
  * with an fp32 running sum), dyn (tiles claimed at run time), k-blocks of 64 per
- * accumulation chunk (num_kb: one chunk), split-K parts (1: none). Returns 0 or a
- * cudaError_t code. */
+ * accumulation chunk (num_kb: one chunk), split-K parts (1: none), A resident in shared
+ * memory over contiguous tile runs (v12 with K <= 512; then `stages` counts B stages).
+ * Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int mode, int num_sms, int *out);
 

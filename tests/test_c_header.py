@@ -12,7 +12,7 @@ PROGRAM = r"""
 #include "vibegemm_b200.h"
 #include <stdio.h>
 int main(void) {
-    int out[19];
+    int out[20];
     int n = vg_b200_num_versions();
     int rc = vg_b200_plan(-1, 8192, 8192, 8192, 256, 256, 256, 0, 148, out);
     printf("%d %s %d %d\n", n, vg_b200_version_name(-1), rc, out[13]);

@@ -30,7 +30,8 @@ def test_versions_and_registry_order(vg):
     assert vg.versions() == ["VibeGEMM B200 v0", "VibeGEMM B200 v1", "VibeGEMM B200 v2",
                              "VibeGEMM B200 v3", "VibeGEMM B200 v4", "VibeGEMM B200 v5",
                              "VibeGEMM B200 v6", "VibeGEMM B200 v7", "VibeGEMM B200 v8",
-                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11"]
+                             "VibeGEMM B200 v9", "VibeGEMM B200 v10", "VibeGEMM B200 v11",
+                             "VibeGEMM B200 v12"]
     assert vg.default_version() == -1 and vg.version_name(-1) == "VibeGEMM B200 auto"
     # cuBLAS registers at priority 0 and is the engine's reference; B200 at priority 3.
     assert vg.backends() == ["cuBLAS"] + vg.versions() + ["VibeGEMM B200 auto"]
@@ -145,6 +146,34 @@ def test_plan_of_run_time_tiles_and_chunks(vg):
     assert vg.plan(-1, 512, 8192, 32768, 256, 256, 256, allgather=True)["version"] == 8
 
 
+def test_plan_of_a_resident(vg):
+    """v12: with K <= 512 (8 k-blocks) A stays in shared memory over each pair's contiguous
+    run of tiles (4 B stages); above that it is v2's plan."""
+    p = vg.plan(12, 8192, 8192, 512, 256, 256, 256)
+    assert (p["a_resident"], p["stages"], p["tile_n"], p["cta_group"], p["grid"]) == (1, 4, 256, 2, 148)
+    assert p["persistent"] == 1 and p["dyn"] == 0 and p["stream_k"] == 0
+    assert vg.plan(12, 512, 512, 520, 256, 256, 256)["a_resident"] == 0  # 9 k-blocks
+    full = vg.plan(12, 8192, 8192, 8192, 256, 256, 256)
+    assert (full["a_resident"], full["stages"]) == (0, 6)
+    for v in range(12):
+        assert vg.plan(v, 8192, 8192, 512, 256, 256, 256)["a_resident"] == 0
+
+
+def test_contiguous_runs_share_row_blocks(vg):
+    """The A-resident schedule: worker w takes tiles [w*T/P, (w+1)*T/P) row-major, so a
+    worker changes A row-block at most ceil(run / num_n) + 1 times."""
+    num_m, num_n, workers = 32, 32, 74
+    seen = []
+    for w in range(workers):
+        units = vg.work_units(2, w, workers, num_m, num_n, 8, 8)
+        lin = [u["tile_m"] * num_n + u["tile_n"] for u in units]
+        assert lin == list(range(1024 * w // workers, 1024 * (w + 1) // workers))
+        rows = {u["tile_m"] for u in units}
+        assert len(rows) <= 2
+        seen += lin
+    assert sorted(seen) == list(range(num_m * num_n))
+
+
 def test_plan_of_split_k(vg):
     """v11: K splits that give every pair slot a unit, >= 8 k-blocks each, and chains of at
     most 64 k-blocks from K = 16384 on; one split (plain v2) when the grid is already full."""
@@ -183,7 +212,7 @@ def test_allgather_plan_never_uses_stream_k(vg):
     with pytest.raises(vg.VibeGemmError):
         vg.plan(4, 501, 1024, 4099, 256, 256, 256, allgather=True)
     import ctypes
-    out = (ctypes.c_int * 19)()
+    out = (ctypes.c_int * 20)()
     assert vg.lib().vg_b200_plan(-1, 512, 1024, 4096, 256, 256, 256, 3, 148, out) != 0  # no mode 3
 
 

@@ -77,7 +77,7 @@ def test_reference_cmake_builds_the_b200_family(tree):
     t, _ = tree
     exe = dropin.build(t, jobs=os.cpu_count() or 8)
     data = exe.read_bytes()
-    for v in [f"v{i}" for i in range(12)] + ["auto"]:
+    for v in [f"v{i}" for i in range(13)] + ["auto"]:
         assert f"VibeGEMM B200 {v}".encode() in data
     # the reference's own cuBLAS backend, compiled with the HAS_B200 arm, is in it too
     assert b"cuBLAS" in data and b"results/perf_b200.txt" in data

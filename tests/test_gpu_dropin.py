@@ -29,7 +29,7 @@ def test_reference_driver_validates_every_b200_backend(tmp_path):
         verdict = re.search(r"max relative error = .*\((PASS|FAIL)\)", body)
         results[name] = (float(tf.group(2)) if tf else None, verdict.group(1) if verdict else None)
     b200 = {k: v for k, v in results.items() if "B200" in k}
-    assert "cuBLAS" in results and len(b200) == 13, results
+    assert "cuBLAS" in results and len(b200) == 14, results
     assert all(v[1] == "PASS" for v in b200.values()), results
     log = (tmp_path / "results" / "perf_b200.txt").read_text()
     assert "VibeGEMM B200 auto" in log

@@ -17,7 +17,7 @@ from conftest import to_dev, to_host
 
 pytestmark = pytest.mark.gpu
 
-VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, -1]  # -1: the default entry point's per-shape choice
+VERSIONS = [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, -1]  # -1: the default entry point's per-shape choice
 # (M, N, K, dist): tails in every dimension, unaligned K (pad path), unaligned N (direct
 # epilogue), single rows/cols, the reference's CPU-checked config 512^3 and config 4b.
 SHAPES = [

@@ -67,7 +67,7 @@ def test_stream_k_plan(vg):
                                    (1000, 3000, 2048), (4096, 14336, 4096), (4096, 4096, 14336),
                                    (8192, 8192, 512), (32768, 32768, 32768), (4096, 32768, 32768),
                                    (256, 2048, 32768), (1000, 3000, 8192)])
-@pytest.mark.parametrize("version", [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11])
+@pytest.mark.parametrize("version", [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12])
 def test_launch_plans_cover_every_iteration_once(vg, shape, version):
     """For the plan the launcher builds (grid, raster group, stream-K or not), the workers'
     units cover every (tile, k-block) iteration of the problem exactly once."""
@@ -93,7 +93,7 @@ def test_launch_plans_cover_every_iteration_once(vg, shape, version):
     workers = p["grid"] // p["cta_group"]
     covered = collections.Counter()
     for w in range(workers):
-        for u in vg.work_units(bool(p["stream_k"]), w, workers, num_m, num_n, p["group_m"], kb,
-                               p["splits"]):
+        mode = 2 if p["a_resident"] else int(p["stream_k"])
+        for u in vg.work_units(mode, w, workers, num_m, num_n, p["group_m"], kb, p["splits"]):
             covered[(u["tile_m"], u["tile_n"])] += u["kb1"] - u["kb0"]
     assert len(covered) == num_m * num_n and set(covered.values()) == {kb}

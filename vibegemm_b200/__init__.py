@@ -65,7 +65,7 @@ EXPORTED_SYMBOLS = tuple(_SIGS)
 
 PLAN_FIELDS = ("cta_group", "stages", "epilogue", "pad_a", "pad_b", "k_padded", "num_m_tiles",
                "num_n_tiles", "num_kb", "group_m", "grid", "persistent", "tile_n", "version", "stream_k",
-               "promote", "dyn", "promote_kb", "splits")
+               "promote", "dyn", "promote_kb", "splits", "a_resident")
 EPILOGUES = {0: "tma_f16", 1: "direct_f16", 2: "direct_f32", 3: "tma_f16_peers", 4: "staged_f16",
              5: "splitk_f16"}
 
@@ -340,9 +340,10 @@ def raster_tile(t: int, num_m: int, num_n: int, group_m: int) -> tuple[int, int]
 UNIT_KINDS = {0: "full", 1: "partial", 2: "owner"}
 
 
-def work_units(stream_k: bool, worker: int, workers: int, num_m: int, num_n: int, group_m: int,
+def work_units(stream_k: int, worker: int, workers: int, num_m: int, num_n: int, group_m: int,
                num_kb: int, splits: int = 1) -> list[dict]:
-    """The units a persistent worker processes (host copy of the device schedule)."""
+    """The units a persistent worker processes (host copy of the device schedule). `stream_k`:
+    0 (or False) grouped raster / split-K, 1 (or True) stream-K, 2 contiguous runs."""
     L = lib()
     n = L.vg_work_units(int(stream_k), worker, workers, num_m, num_n, group_m, num_kb, splits, None, 0)
     if n < 0:

@@ -156,23 +156,30 @@ template <int NSUB> __host__ __device__ __forceinline__ int acc_col_to_c(int t) 
         return ((t & 255) >> 7 << 8) + ((t >> 8) << 7) + (t & 127);
 }
 
-template <int CG, int BN, int STAGES, int EPI> struct SmemLayout {
+// A-resident kernels (ARES) keep a CTA's whole A row-block of K <= kAresMaxKb k-blocks in
+// shared memory, one slot per k-block, and stream only B through the pipeline stages.
+constexpr int kAresMaxKb = 8;
+
+template <int CG, int BN, int STAGES, int EPI, bool ARES = false> struct SmemLayout {
     using T = TileCfg<CG, BN>;
+    static constexpr int A_SLOTS = ARES ? kAresMaxKb : STAGES;
     static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = A_OFF + STAGES * T::A_BYTES;
+    static constexpr int B_OFF = A_OFF + A_SLOTS * T::A_BYTES;
     static constexpr int EPI_OFF = B_OFF + STAGES * T::B_BYTES;
     // Staging boxes per epilogue warp: two (a TMA store drains while the next box is
     // written) unless that would not leave room for the pipeline stages.
     static constexpr int kSmemLimit = 232448; // 227 KB of dynamic shared memory per CTA
     static constexpr int EPI_BUFS =
-        (STAGES * (T::A_BYTES + T::B_BYTES) + T::EPI_WARPS * 2 * T::STG_BYTES + 2048 <= kSmemLimit) ? 2 : 1;
+        (A_SLOTS * T::A_BYTES + STAGES * T::B_BYTES + T::EPI_WARPS * 2 * T::STG_BYTES + 2048 <= kSmemLimit)
+            ? 2
+            : 1;
     static constexpr int EPI_BYTES = (EPI == kEpiTmaF16 || EPI == kEpiTmaF16Peers || EPI == kEpiStagedF16)
                                          ? T::EPI_WARPS * EPI_BUFS * T::STG_BYTES
                                          : 0;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
-    // full/empty per stage, tfull/tempty per accumulator, drain, then the DYN ring's
-    // full/empty per entry.
-    static constexpr int NUM_BARS = 2 * STAGES + 4 + 1 + 2 * kSchedDepth;
+    // full/empty per stage, tfull/tempty per accumulator, drain, the DYN ring's full/empty
+    // per entry, then (ARES) full/empty per A slot.
+    static constexpr int NUM_BARS = 2 * STAGES + 4 + 1 + 2 * kSchedDepth + (ARES ? 2 * kAresMaxKb : 0);
     static constexpr int SLOT_OFF = BAR_OFF + 8 * NUM_BARS;
     static constexpr int ABORT_OFF = SLOT_OFF + 4;
     static constexpr int RING_OFF = ABORT_OFF + 4; // int tile[kSchedDepth]
@@ -286,15 +293,25 @@ __device__ __forceinline__ bool wait_flag(const unsigned *f, volatile int *abort
 // CTAs take it (full/empty mbarriers per entry; the peer's roles arrive remotely). Pairs that
 // finish early take more tiles, as with hardware-placed pairs, while the epilogue of one
 // tile still overlaps the next tile's main loop.
-template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false, bool DYN = false>
+//
+// ARES (A resident; the 256×256 pair with K <= kAresMaxKb k-blocks): each pair walks a
+// contiguous run of tiles in row-major order, so consecutive tiles share their A row-block.
+// The producer loads A once per row-block into per-k-block slots (slot k waits for the MMA
+// issuer to have finished the previous row-block's last use of it) and streams only B
+// through the stages; the MMA issuer frees the slots after the last tile of a row-block.
+template <int CG, int BN, int STAGES, int EPI, bool SK = false, bool PROMOTE = false, bool DYN = false,
+          bool ARES = false>
 __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREADS), 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap mapA,
                      const __grid_constant__ CUtensorMap mapB,
                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
     using T = TileCfg<CG, BN, PROMOTE && BN == 512>;
-    using L = SmemLayout<CG, BN, STAGES, EPI>;
+    using L = SmemLayout<CG, BN, STAGES, EPI, ARES>;
     static_assert(L::T::EPI_WARPS == T::EPI_WARPS, "shared-memory layout sized for these warps");
+    static_assert(!ARES || (CG == 2 && BN == 256 && !SK && !PROMOTE && !DYN),
+                  "A-resident: the 256x256 pair tile with the static walk");
+    constexpr int kUnitMode = SK ? kModeStreamK : (ARES ? kModeContiguous : kModeRaster);
     // Single-accumulator tiles of the static walk (v3, v6) end half by half (tfull(0), then
     // tfull(1)). Measured at 8192³: +0.4–0.7 % (burst 1514–1520 vs 1509–1510 TFLOP/s, sustained
     // 1307–1312 vs 1302–1306); with run-time claims at 32768³ (v10) it lost 1.5 % sustained.
@@ -327,6 +344,8 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
     const uint32_t drain_bar = sBar + 8u * (2 * STAGES + 4);
     auto sfull_bar = [&](int i) { return sBar + 8u * (2 * STAGES + 5 + i); };
     auto sempty_bar = [&](int i) { return sBar + 8u * (2 * STAGES + 5 + kSchedDepth + i); };
+    auto afull_bar = [&](int k) { return sBar + 8u * (2 * STAGES + 5 + 2 * kSchedDepth + k); };
+    auto aempty_bar = [&](int k) { return sBar + 8u * (2 * STAGES + 5 + 2 * kSchedDepth + kAresMaxKb + k); };
     const uint32_t ring = base + L::RING_OFF;
 
     if (threadIdx.x == 0) {
@@ -339,6 +358,12 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
             ptx::mbar_init(tempty_bar(a), T::EPI_WARPS * CG);
         }
         ptx::mbar_init(drain_bar, 1);
+        if constexpr (ARES) {
+            for (int k = 0; k < kAresMaxKb; ++k) {
+                ptx::mbar_init(afull_bar(k), 1);
+                ptx::mbar_init(aempty_bar(k), 1);
+            }
+        }
         // DYN ring (leader's entries are released by: its MMA thread, its epilogue warps,
         // the peer's producer and the peer's epilogue warps).
         for (int i = 0; i < kSchedDepth; ++i) {
@@ -436,7 +461,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                 int issued = 0;
                 bool ok = true;
                 UnitIter it;
-                it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                it.init(kUnitMode, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                         args.num_kb, args.splits);
                 WorkUnit u;
                 auto next_unit = [&]() -> bool {
@@ -451,17 +476,45 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         return it.next(u);
                     }
                 };
+                int a_gen = 0;            // ARES: A row-blocks loaded so far
+                int a_m = -1;             // ARES: the row-block in the slots
+                uint32_t a_used = 0;      // ARES: slots ever loaded
+                uint32_t a_par = 0;       // ARES: parity of each slot's latest load
                 while (ok && next_unit()) {
                     const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
                     const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
+                    const bool load_a = ARES && u.tile_m != a_m;
                     for (int kb = u.kb0; kb < u.kb1; ++kb) {
+                        if constexpr (ARES) {
+                            if (load_a) {
+                                // Slot kb is free once the MMAs of the previous row-block's
+                                // last tile have read it.
+                                if (!wait_bar<T::RSUM>(aempty_bar(kb), (static_cast<uint32_t>(a_gen) & 1u) ^ 1u,
+                                                       abort_flag, tmo, kStatusTimeoutProducer)) {
+                                    ok = false;
+                                    break;
+                                }
+                                const uint32_t ab = afull_bar(kb);
+                                if (rank == 0)
+                                    ptx::mbar_arrive_expect_tx(ab, CG * T::A_BYTES);
+                                ptx::tma_load_2d_pair(sA + kb * T::A_BYTES, &mapA, ptx::mapa(ab, 0), kb * T::BK,
+                                                      a_row);
+                                a_used |= 1u << kb;
+                                a_par = (a_par & ~(1u << kb)) | ((static_cast<uint32_t>(a_gen) & 1u) << kb);
+                            }
+                        }
                         if (!wait_bar<T::RSUM>(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
                                       kStatusTimeoutProducer)) {
                             ok = false;
                             break;
                         }
                         const uint32_t fb = full_bar(stage);
-                        if constexpr (CG == 1) {
+                        if constexpr (ARES) {
+                            if (rank == 0)
+                                ptx::mbar_arrive_expect_tx(fb, CG * T::B_BYTES);
+                            ptx::tma_load_2d_pair(sB + stage * T::B_BYTES, &mapB, ptx::mapa(fb, 0), kb * T::BK,
+                                                  b_row);
+                        } else if constexpr (CG == 1) {
                             ptx::mbar_arrive_expect_tx(fb, T::STAGE_TX);
                             ptx::tma_load_2d(sA + stage * T::A_BYTES, &mapA, fb, kb * T::BK, a_row);
                             ptx::tma_load_2d(sB + stage * T::B_BYTES, &mapB, fb, kb * T::BK, b_row);
@@ -478,6 +531,22 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1u;
+                        }
+                    }
+                    if (load_a) {
+                        a_m = u.tile_m;
+                        ++a_gen;
+                    }
+                }
+                // ARES: the latest load of every slot must have landed before this CTA exits
+                // (true on the normal path, where the MMAs read them; bounded otherwise).
+                if (ARES && rank == 0 && !ok) {
+                    for (int k = 0; k < kAresMaxKb; ++k) {
+                        if (!((a_used >> k) & 1u))
+                            continue;
+                        const uint32_t par = (a_par >> k) & 1u;
+                        const uint64_t t0 = ptx::global_timer_ns();
+                        while (!ptx::mbar_try_wait(afull_bar(k), par) && ptx::global_timer_ns() - t0 < tmo) {
                         }
                     }
                 }
@@ -510,6 +579,8 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                 uint32_t acc_phase = 0;
                 bool ok = true;
                 bool any = false;
+                int a_m = -1;  // ARES: the row-block whose A is in the slots
+                int a_gen = 0; // ARES: row-blocks started
                 auto advance = [&]() {
                     if (++stage == STAGES) {
                         stage = 0;
@@ -519,7 +590,8 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                 // MMAs of one k-block for accumulator half `h` (columns [256h, 256h+256)). `kb` counts
                 // the k-blocks of the accumulation run: at 0 the first MMA overwrites D.
                 auto issue = [&](uint32_t d, int h, int kb) {
-                    const uint64_t a0 = ptx::smem_desc_k_sw128(sA + stage * T::A_BYTES);
+                    // ARES: A from the resident slot of k-block kb, B from the stage.
+                    const uint64_t a0 = ptx::smem_desc_k_sw128(sA + (ARES ? kb : stage) * T::A_BYTES);
                     const uint64_t b0 = ptx::smem_desc_k_sw128(sB + stage * T::B_BYTES + h * T::B_SUB_BYTES);
 #pragma unroll
                     for (int k = 0; k < T::BK / 16; ++k) {
@@ -535,7 +607,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         ptx::mma_commit_pair(bar, 0x3);
                 };
                 UnitIter it;
-                it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+                it.init(kUnitMode, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                         args.num_kb, args.splits);
                 WorkUnit u;
                 auto next_unit = [&]() -> bool {
@@ -587,7 +659,24 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         }
                         ptx::tc_fence_after();
                         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * T::ACC_STRIDE);
+                        // ARES: the row-block's generation (its slots' full phase) and whether
+                        // this tile is its last user (then its MMAs free the slots).
+                        bool a_last = false;
+                        if constexpr (ARES) {
+                            if (u.tile_m != a_m) {
+                                a_m = u.tile_m;
+                                ++a_gen;
+                            }
+                            a_last = it.last_of_row(u.tile_m);
+                        }
                         for (int kb = 0; kb < nkb; ++kb) {
+                            if constexpr (ARES) {
+                                if (!wait_bar<T::RSUM>(afull_bar(kb), static_cast<uint32_t>(a_gen - 1) & 1u,
+                                                       abort_flag, tmo, kStatusTimeoutMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                            }
                             if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
                                 ok = false;
                                 break;
@@ -596,6 +685,8 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             issue(d, 0, kb);
                             any = true;
                             commit_to(empty_bar(stage));
+                            if (ARES && a_last)
+                                commit_to(aempty_bar(kb));
                             advance();
                         }
                         if (!ok)
@@ -727,7 +818,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
         uint32_t acc_phase = 0;
         int buf = 0;
         UnitIter it;
-        it.init(SK, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
+        it.init(kUnitMode, cluster_id, num_clusters, args.num_m_tiles, args.num_n_tiles, args.group_m,
                 args.num_kb, args.splits);
         WorkUnit u;
         // Stream-K partial slot of (worker, CTA rank): 128 × BN floats.

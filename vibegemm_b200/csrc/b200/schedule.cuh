@@ -48,6 +48,10 @@ VG_HD void raster_tile(int t, int num_m, int num_n, int group_m, int &tile_m, in
 //                  stores C. A worker's partial unit can only be its first unit and its
 //                  owner unit only its last, so an owner waits only on later workers'
 //                  first units: no cycle.
+//   contiguous:    worker w takes the whole tiles [w·T/P, (w+1)·T/P) in row-major order
+//                  (tile_n fastest), so consecutive tiles of a worker share their A
+//                  row-block (the A-resident kernel keeps it in shared memory).
+enum UnitMode : int { kModeRaster = 0, kModeStreamK = 1, kModeContiguous = 2 };
 enum UnitKind : int { kUnitFull = 0, kUnitPartial = 1, kUnitOwner = 2 };
 
 struct WorkUnit {
@@ -57,14 +61,17 @@ struct WorkUnit {
 };
 
 struct UnitIter {
+    int mode;
     bool sk;
     int w, P, num_m, num_n, group_m, KB, S;
     long long i, end, W; // stream-K position
     int t;               // data-parallel position
+    int t_end;           // contiguous: one past this worker's last tile
 
-    VG_HD void init(bool stream_k, int worker, int workers, int nm, int nn, int gm, int kb,
+    VG_HD void init(int unit_mode, int worker, int workers, int nm, int nn, int gm, int kb,
                     int splits = 1) {
-        sk = stream_k;
+        mode = unit_mode;
+        sk = unit_mode == kModeStreamK;
         w = worker;
         P = workers;
         num_m = nm;
@@ -76,12 +83,33 @@ struct UnitIter {
         i = begin_of(w);
         end = begin_of(w + 1);
         t = w;
+        if (mode == kModeContiguous) {
+            const long long T = (long long)nm * nn;
+            t = (int)(T * w / P);
+            t_end = (int)(T * (w + 1) / P);
+        }
     }
+    // Contiguous mode: whether the tile `next` returns after the current one (if any) is in
+    // a different M row-block, i.e. the current tile is the last user of its A row-block.
+    VG_HD bool last_of_row(int tile_m) const { return t >= t_end || t / num_n != tile_m; }
     VG_HD long long begin_of(int worker) const { return (long long)worker * W / P; }
     // Worker whose range contains iteration index `idx`.
     VG_HD int worker_of(long long idx) const { return (int)(((idx + 1) * P + W - 1) / W) - 1; }
 
     VG_HD bool next(WorkUnit &u) {
+        if (mode == kModeContiguous) {
+            if (t >= t_end)
+                return false;
+            u.tile_m = t / num_n;
+            u.tile_n = t - u.tile_m * num_n;
+            u.kb0 = 0;
+            u.kb1 = KB;
+            u.kind = kUnitFull;
+            u.first_contrib = u.last_contrib = -1;
+            u.split = 0;
+            ++t;
+            return true;
+        }
         if (!sk) {
             const int T = num_m * num_n;
             if (t >= T * S)

@@ -71,6 +71,7 @@ struct VersionDesc {
     bool promote = false; // chunked accumulation with an fp32 running sum (accurate long K)
     bool dyn = false;     // tiles claimed at run time (atomic counter) by the persistent pairs
     bool split_k = false; // K range split over several units, fp32 partials + reduction kernel
+    bool a_resident = false; // K <= 512: A row-block kept in shared memory over contiguous tile runs
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -88,6 +89,9 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 8, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
+    // v12: v2's tile and double-buffered TMEM with A resident in shared memory for K <= 512
+    // (4 B stages); above that it runs as v2.
+    {"VibeGEMM B200 v12", 2, 256, 4, true, true, 8, false, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -223,6 +227,7 @@ struct Plan {
     int dyn = 0;
     int promote_kb = 0; // k-blocks per accumulation chunk (num_kb: one chunk)
     int splits = 1;     // split-K parts (1: none)
+    int a_resident = 0; // A row-block resident in shared memory (stages = B stages)
 };
 
 inline bool aligned16(uintptr_t p) { return (p & 15u) == 0; }
@@ -269,6 +274,12 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.dyn = v.dyn ? 1 : 0;
     p.promote_kb = v.promote ? promote_chunk_kb(v.cta_group == 2 && v.bn == 512 ? 2 : 1, p.num_kb, p.Kp)
                              : p.num_kb;
+    if (v.a_resident) {
+        if (p.num_kb <= kAresMaxKb)
+            p.a_resident = 1;
+        else
+            p.stages = 6; // v2's pipeline
+    }
     if (v.split_k) {
         // Enough K splits to give every slot (pair or SM) a unit (one wave), at least 8
         // k-blocks per split, and from K = kPromoteMinK on chains of at most kPromoteKb k-blocks.
@@ -554,16 +565,16 @@ cudaError_t launch_splitk_reduce(const float *ws, int S, int M, int N, void *C, 
 }
 
 // ── kernel launch ────────────────────────────────────────────────────────────
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> struct Inst {
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN, bool ARES> struct Inst {
     using T = TileCfg<CG, BN, PROMOTE && BN == 512>;
-    static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI>::DYN_BYTES;
+    static constexpr int kSmem = SmemLayout<CG, BN, STAGES, EPI, ARES>::DYN_BYTES;
     static std::atomic<unsigned long long> attr_ready; // bit per device
     static int max_clusters[kMaxDevices];
 
     static cudaError_t prepare(int dev) {
         if ((attr_ready.load(std::memory_order_acquire) >> dev) & 1ull)
             return cudaSuccess;
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN, ARES>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
@@ -601,7 +612,7 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> 
 
     static cudaError_t launch(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                               const GemmArgs &args, int grid, cudaStream_t s) {
-        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>;
+        auto kern = &gemm_f16_tcgen05<CG, BN, STAGES, EPI, SK, PROMOTE, DYN, ARES>;
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid, 1, 1);
         cfg.blockDim = dim3(T::THREADS, 1, 1);
@@ -626,24 +637,25 @@ template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN> 
         return cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, args);
     }
 };
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN>
-std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>::attr_ready{0};
-template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN>
-int Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN>::max_clusters[kMaxDevices] = {};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN, bool ARES>
+std::atomic<unsigned long long> Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN, ARES>::attr_ready{0};
+template <int CG, int BN, int STAGES, int EPI, bool SK, bool PROMOTE, bool DYN, bool ARES>
+int Inst<CG, BN, STAGES, EPI, SK, PROMOTE, DYN, ARES>::max_clusters[kMaxDevices] = {};
 
-template <int CG, int BN, int STAGES, bool SK = false, bool PROMOTE = false, bool DYN = false>
+template <int CG, int BN, int STAGES, bool SK = false, bool PROMOTE = false, bool DYN = false,
+          bool ARES = false>
 cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
                          const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                          const GemmArgs *args, int grid, cudaStream_t s) {
 #define VG_EPI_CASE(E)                                                                             \
     case E: {                                                                                      \
-        cudaError_t e = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::prepare(dev);                   \
+        cudaError_t e = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN, ARES>::prepare(dev);                   \
         if (e != cudaSuccess)                                                                      \
             return e;                                                                              \
-        max_clusters = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::max_clusters[dev];               \
+        max_clusters = Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN, ARES>::max_clusters[dev];               \
         if (query_only)                                                                            \
             return cudaSuccess;                                                                    \
-        return Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN>::launch(*ma, *mb, *mc, *args, grid, s);   \
+        return Inst<CG, BN, STAGES, E, SK, PROMOTE, DYN, ARES>::launch(*ma, *mb, *mc, *args, grid, s);   \
     }
     if constexpr (SK) {
         switch (epi) {
@@ -671,6 +683,9 @@ cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
 cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
                      const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                      const GemmArgs *args, int grid, cudaStream_t s) {
+    if (p.a_resident) // v12 with K <= 512
+        return dispatch_epi<2, 256, 4, false, false, false, true>(p.epi, dev, max_clusters, query_only, ma, mb,
+                                                                  mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 256 && p.stages == 4)
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 192 && p.stages == 4)
@@ -1096,10 +1111,11 @@ void vg_shard_rows(long long M, int world, int rank, long long *row0, long long 
 int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, int group_m,
                   int num_kb, int splits, int *out, int max_units) {
     if (worker < 0 || workers <= 0 || worker >= workers || num_m <= 0 || num_n <= 0 ||
-        group_m <= 0 || num_kb <= 0 || max_units < 0 || splits < 1 || (stream_k && splits != 1))
+        group_m <= 0 || num_kb <= 0 || max_units < 0 || splits < 1 || stream_k < 0 || stream_k > 2 ||
+        (stream_k != 0 && splits != 1))
         return -1;
     vg::UnitIter it;
-    it.init(stream_k != 0, worker, workers, num_m, num_n, group_m, num_kb, splits);
+    it.init(stream_k, worker, workers, num_m, num_n, group_m, num_kb, splits);
     vg::WorkUnit u;
     int n = 0;
     while (it.next(u)) {
@@ -1138,10 +1154,10 @@ int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uin
                                 mode == 2);
     if (e != 0 || !out)
         return e ? e : (int)cudaErrorInvalidValue;
-    const int vals[19] = {p.cta_group, p.stages,      p.epi,         p.pad_a,  p.pad_b,
-                          p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb, p.group_m,
+    const int vals[20] = {p.cta_group, p.stages,      p.epi,         p.pad_a,   p.pad_b,
+                          p.Kp,        p.num_m_tiles, p.num_n_tiles, p.num_kb,  p.group_m,
                           p.grid,      p.persistent,  p.bn,          p.version, p.stream_k,
-                          p.promote,   p.dyn,         p.promote_kb,  p.splits};
+                          p.promote,   p.dyn,         p.promote_kb,  p.splits,  p.a_resident};
     std::memcpy(out, vals, sizeof(vals));
     return 0;
 }

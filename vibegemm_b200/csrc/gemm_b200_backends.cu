@@ -64,6 +64,9 @@ void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_versi
 namespace gemm_b200_v11 {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<11>(A, B, C, M, N, K); }
 } // namespace gemm_b200_v11
+namespace gemm_b200_v12 {
+void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<12>(A, B, C, M, N, K); }
+} // namespace gemm_b200_v12
 // The default entry point: one of the versions above, chosen per shape.
 namespace gemm_b200_auto {
 void launchKernel(half *A, half *B, half *C, int M, int N, int K) { launch_version<-1>(A, B, C, M, N, K); }
@@ -104,4 +107,5 @@ REGISTER_B200_KERNEL("VibeGEMM B200 v8", GeneratedB200KernelBackend<gemm_b200_v8
 REGISTER_B200_KERNEL("VibeGEMM B200 v9", GeneratedB200KernelBackend<gemm_b200_v9::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v10", GeneratedB200KernelBackend<gemm_b200_v10::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 v11", GeneratedB200KernelBackend<gemm_b200_v11::launchKernel>);
+REGISTER_B200_KERNEL("VibeGEMM B200 v12", GeneratedB200KernelBackend<gemm_b200_v12::launchKernel>);
 REGISTER_B200_KERNEL("VibeGEMM B200 auto", GeneratedB200KernelBackend<gemm_b200_auto::launchKernel>);
