@@ -480,6 +480,9 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                 int a_m = -1;             // ARES: the row-block in the slots
                 uint32_t a_used = 0;      // ARES: slots ever loaded
                 uint32_t a_par = 0;       // ARES: parity of each slot's latest load
+                auto producer_wait = [&](uint32_t bar, uint32_t parity) {
+                    return wait_bar<T::RSUM>(bar, parity, abort_flag, tmo, kStatusTimeoutProducer);
+                };
                 while (ok && next_unit()) {
                     const int a_row = u.tile_m * (T::BM * CG) + static_cast<int>(rank) * T::BM;
                     const int b_row = u.tile_n * T::BN + static_cast<int>(rank) * T::B_ROWS;
@@ -489,8 +492,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             if (load_a) {
                                 // Slot kb is free once the MMAs of the previous row-block's
                                 // last tile have read it.
-                                if (!wait_bar<T::RSUM>(aempty_bar(kb), (static_cast<uint32_t>(a_gen) & 1u) ^ 1u,
-                                                       abort_flag, tmo, kStatusTimeoutProducer)) {
+                                if (!producer_wait(aempty_bar(kb), (static_cast<uint32_t>(a_gen) & 1u) ^ 1u)) {
                                     ok = false;
                                     break;
                                 }
@@ -503,8 +505,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                                 a_par = (a_par & ~(1u << kb)) | ((static_cast<uint32_t>(a_gen) & 1u) << kb);
                             }
                         }
-                        if (!wait_bar<T::RSUM>(empty_bar(stage), phase ^ 1u, abort_flag, tmo,
-                                      kStatusTimeoutProducer)) {
+                        if (!producer_wait(empty_bar(stage), phase ^ 1u)) {
                             ok = false;
                             break;
                         }
@@ -581,6 +582,9 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                 bool any = false;
                 int a_m = -1;  // ARES: the row-block whose A is in the slots
                 int a_gen = 0; // ARES: row-blocks started
+                auto mma_wait = [&](uint32_t bar, uint32_t parity) {
+                    return wait_bar<T::RSUM>(bar, parity, abort_flag, tmo, kStatusTimeoutMma);
+                };
                 auto advance = [&]() {
                     if (++stage == STAGES) {
                         stage = 0;
@@ -627,14 +631,13 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                     if constexpr (PROMOTE && T::ACC_BUFS == 2) {
                         for (int c0 = 0; c0 < nkb && ok; c0 += args.promote_kb) {
                             const int c1 = min(nkb, c0 + args.promote_kb);
-                            if (!wait_bar<T::RSUM>(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo,
-                                          kStatusTimeoutMma)) {
+                            if (!mma_wait(tempty_bar(0), acc_phase ^ 1u)) {
                                 ok = false;
                                 break;
                             }
                             ptx::tc_fence_after();
                             for (int kb = c0; kb < c1; ++kb) {
-                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                if (!mma_wait(full_bar(stage), phase)) {
                                     ok = false;
                                     break;
                                 }
@@ -652,8 +655,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         if (!ok)
                             break;
                     } else if constexpr (T::ACC_BUFS == 2) {
-                        if (!wait_bar<T::RSUM>(tempty_bar(acc), acc_phase ^ 1u, abort_flag, tmo,
-                                      kStatusTimeoutMma)) {
+                        if (!mma_wait(tempty_bar(acc), acc_phase ^ 1u)) {
                             ok = false;
                             break;
                         }
@@ -671,13 +673,12 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         }
                         for (int kb = 0; kb < nkb; ++kb) {
                             if constexpr (ARES) {
-                                if (!wait_bar<T::RSUM>(afull_bar(kb), static_cast<uint32_t>(a_gen - 1) & 1u,
-                                                       abort_flag, tmo, kStatusTimeoutMma)) {
+                                if (!mma_wait(afull_bar(kb), static_cast<uint32_t>(a_gen - 1) & 1u)) {
                                     ok = false;
                                     break;
                                 }
                             }
-                            if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                            if (!mma_wait(full_bar(stage), phase)) {
                                 ok = false;
                                 break;
                             }
@@ -710,7 +711,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                         for (int c0 = 0; c0 < nkb && ok; c0 += chunk) {
                             const int n = (nkb - c0) < chunk ? (nkb - c0) : chunk;
                             const int kb_base = (PROMOTE && c0 > 0) ? 1 : 0; // carry: accumulate
-                            if (!wait_bar<T::RSUM>(tempty_bar(0), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
+                            if (!mma_wait(tempty_bar(0), acc_phase ^ 1u)) {
                                 ok = false;
                                 break;
                             }
@@ -719,7 +720,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             const int s0 = stage;
                             const uint32_t p0 = phase;
                             for (int kb = 0; kb < run; ++kb) {
-                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                if (!mma_wait(full_bar(stage), phase)) {
                                     ok = false;
                                     break;
                                 }
@@ -730,7 +731,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             }
                             if (!ok)
                                 break;
-                            if (!wait_bar<T::RSUM>(tempty_bar(1), acc_phase ^ 1u, abort_flag, tmo, kStatusTimeoutMma)) {
+                            if (!mma_wait(tempty_bar(1), acc_phase ^ 1u)) {
                                 ok = false;
                                 break;
                             }
@@ -744,7 +745,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                             }
                             const int tail = kHalfEnds ? min(n - run, STAGES / 2) : 0;
                             for (int kb = run; kb < n - tail; ++kb) {
-                                if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo, kStatusTimeoutMma)) {
+                                if (!mma_wait(full_bar(stage), phase)) {
                                     ok = false;
                                     break;
                                 }
@@ -760,8 +761,7 @@ __global__ void __launch_bounds__((TileCfg<CG, BN, PROMOTE && BN == 512>::THREAD
                                 const int s1 = stage;
                                 const uint32_t p1 = phase;
                                 for (int kb = n - tail; kb < n; ++kb) {
-                                    if (!wait_bar<T::RSUM>(full_bar(stage), phase, abort_flag, tmo,
-                                                           kStatusTimeoutMma)) {
+                                    if (!mma_wait(full_bar(stage), phase)) {
                                         ok = false;
                                         break;
                                     }
