@@ -90,6 +90,7 @@ def test_plan_aligned_square(vg):
     ((4096, 4096, 14336), 3),
     ((8191, 8193, 4099), 3),     # 7.4 vs 14.3 waves: estimates within 1.5 %, v3's data saving wins
     ((8192, 8192, 512), 2),      # short K: double-buffered accumulator
+    ((8192, 8192, 256), 12),     # K <= 256: the same tile with A resident in shared memory
     ((1000, 3000, 2048), 5),     # fewer pair tiles than pair slots: 128x192 tiles fill one wave
     ((1000, 3000, 8192), 7),     # same tiles, long K: the fifth stage pays
     ((512, 512, 512), 5),

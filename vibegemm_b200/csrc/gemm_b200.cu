@@ -153,8 +153,12 @@ int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
         const double e2 = (double)((t2 + pairs - 1) / pairs) * 256;
         return e3 <= 1.015 * e2 ? 3 : 2;
     }
+    // Short K over at least a wave of 256×256 tiles: v2, or at K <= 256 v12, v2's tile with A
+    // resident in shared memory (measured against v2, TFLOP/s burst / sustained: 8192²×256
+    // 827 / 715 vs 804 / 685, 8192²×128 466 / 440 vs 453 / 422, 4096×14336×256 736 / 671 vs
+    // 725 / 645, 16384×8192×256 838 / 727 vs 840 / 713; at K = 384 and 512 v2 is level or ahead).
     if (t2 >= pairs)
-        return 2;
+        return K <= 256 ? 12 : 2;
     // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
     // (v1), pair 256×256 (v2), 128×192 (v5) and a K split over pair tiles (estimated as
     // stream-K, v4, whose split tiles pay a fix-up of about 28 k-blocks: partials out, owner
