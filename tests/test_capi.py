@@ -145,6 +145,9 @@ def test_plan_of_run_time_tiles_and_chunks(vg):
     p = vg.plan(-1, 4096, 32768, 32768, 256, 256, 256, allgather=True)
     assert p["version"] == 9 and p["epilogue"] == "tma_f16_peers"
     assert vg.plan(-1, 512, 8192, 32768, 256, 256, 256, allgather=True)["version"] == 8
+    # at K <= 256 the fused all-gather keeps v2 (the default entry point takes v12)
+    assert vg.plan(-1, 8192, 8192, 256, 256, 256, 256, allgather=True)["version"] == 2
+    assert vg.plan(-1, 8192, 8192, 256, 256, 256, 256)["version"] == 12
 
 
 def test_plan_of_a_resident(vg):

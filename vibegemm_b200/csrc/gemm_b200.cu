@@ -126,6 +126,8 @@ int promote_chunk_kb(int version_promote_kind, int num_kb, int Kp) {
 // (v7: one staging box per epilogue warp; +14 % at 1000×3000×8192, -3..5 % at K <= 2048,
 // where the shorter epilogue matters more) and stream-K (v4, only for long K over few
 // tiles: its fp32 fix-up costs about 28 k-blocks per split tile).
+// `allow_split` is false for the fused all-gather, which has no split-K or stream-K form and
+// keeps v2 at short K.
 int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     const long long pairs = num_sms / 2;
     const long long t3 = (long long)ceil_div_i(M, 256) * ceil_div_i(N, 512);
@@ -157,8 +159,9 @@ int select_version(int M, int N, int K, int num_sms, bool allow_split = true) {
     // resident in shared memory (measured against v2, TFLOP/s burst / sustained: 8192²×256
     // 827 / 715 vs 804 / 685, 8192²×128 466 / 440 vs 453 / 422, 4096×14336×256 736 / 671 vs
     // 725 / 645, 16384×8192×256 838 / 727 vs 840 / 713; at K = 384 and 512 v2 is level or ahead).
+    // (The fused all-gather keeps v2 there: its peer-store epilogue is tested on v2's schedule.)
     if (t2 >= pairs)
-        return K <= 256 ? 12 : 2;
+        return (K <= 256 && allow_split) ? 12 : 2;
     // Under-filled grid: estimated time in (tile columns × k-blocks) per SM for 128×256
     // (v1), pair 256×256 (v2), 128×192 (v5) and a K split over pair tiles (estimated as
     // stream-K, v4, whose split tiles pay a fix-up of about 28 k-blocks: partials out, owner
