@@ -204,7 +204,7 @@ int vg_work_units(int stream_k, int worker, int workers, int num_m, int num_n, i
  * persistent, tile columns, resolved version, stream-K, promote (chunked accumulation
  * with an fp32 running sum), dyn (tiles claimed at run time), k-blocks of 64 per
  * accumulation chunk (num_kb: one chunk), split-K parts (1: none), A resident in shared
- * memory over contiguous tile runs (v12 with K <= 512; then `stages` counts B stages).
+ * memory over contiguous tile runs (v12 with K <= 256; then `stages` counts B stages).
  * Returns 0 or a cudaError_t code. */
 int vg_b200_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintptr_t C,
                  int mode, int num_sms, int *out);

@@ -151,12 +151,13 @@ def test_plan_of_run_time_tiles_and_chunks(vg):
 
 
 def test_plan_of_a_resident(vg):
-    """v12: with K <= 512 (8 k-blocks) A stays in shared memory over each pair's contiguous
-    run of tiles (4 B stages); above that it is v2's plan."""
-    p = vg.plan(12, 8192, 8192, 512, 256, 256, 256)
-    assert (p["a_resident"], p["stages"], p["tile_n"], p["cta_group"], p["grid"]) == (1, 4, 256, 2, 148)
+    """v12: with K <= 256 (4 k-blocks) A stays in shared memory over each pair's contiguous
+    run of tiles (6 B stages); above that it is v2's plan."""
+    p = vg.plan(12, 8192, 8192, 256, 256, 256, 256)
+    assert (p["a_resident"], p["stages"], p["tile_n"], p["cta_group"], p["grid"]) == (1, 6, 256, 2, 148)
     assert p["persistent"] == 1 and p["dyn"] == 0 and p["stream_k"] == 0
-    assert vg.plan(12, 512, 512, 520, 256, 256, 256)["a_resident"] == 0  # 9 k-blocks
+    assert vg.plan(12, 512, 512, 264, 256, 256, 256)["a_resident"] == 0  # 5 k-blocks
+    assert vg.plan(12, 8192, 8192, 512, 256, 256, 256)["a_resident"] == 0
     full = vg.plan(12, 8192, 8192, 8192, 256, 256, 256)
     assert (full["a_resident"], full["stages"]) == (0, 6)
     for v in range(12):

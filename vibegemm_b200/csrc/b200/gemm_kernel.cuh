@@ -157,8 +157,9 @@ template <int NSUB> __host__ __device__ __forceinline__ int acc_col_to_c(int t) 
 }
 
 // A-resident kernels (ARES) keep a CTA's whole A row-block of K <= kAresMaxKb k-blocks in
-// shared memory, one slot per k-block, and stream only B through the pipeline stages.
-constexpr int kAresMaxKb = 8;
+// shared memory, one slot per k-block, and stream only B through the pipeline stages. Four
+// slots (64 KB) leave room for six 16 KB B stages and two staging boxes per epilogue warp.
+constexpr int kAresMaxKb = 4;
 
 template <int CG, int BN, int STAGES, int EPI, bool ARES = false> struct SmemLayout {
     using T = TileCfg<CG, BN>;

@@ -71,7 +71,7 @@ struct VersionDesc {
     bool promote = false; // chunked accumulation with an fp32 running sum (accurate long K)
     bool dyn = false;     // tiles claimed at run time (atomic counter) by the persistent pairs
     bool split_k = false; // K range split over several units, fp32 partials + reduction kernel
-    bool a_resident = false; // K <= 512: A row-block kept in shared memory over contiguous tile runs
+    bool a_resident = false; // K <= 256: A row-block kept in shared memory over contiguous tile runs
 };
 
 constexpr VersionDesc kVersions[] = {
@@ -89,9 +89,9 @@ constexpr VersionDesc kVersions[] = {
     {"VibeGEMM B200 v9", 2, 512, 4, true, true, 8, false, true, true},
     {"VibeGEMM B200 v10", 2, 512, 4, true, true, 16, false, false, true},
     {"VibeGEMM B200 v11", 2, 256, 6, true, true, 8, false, false, false, true},
-    // v12: v2's tile and double-buffered TMEM with A resident in shared memory for K <= 512
-    // (4 B stages); above that it runs as v2.
-    {"VibeGEMM B200 v12", 2, 256, 4, true, true, 8, false, false, false, false, true},
+    // v12: v2's tile and double-buffered TMEM with A resident in shared memory for K <= 256
+    // (6 B stages); above that it runs as v2.
+    {"VibeGEMM B200 v12", 2, 256, 6, true, true, 8, false, false, false, false, true},
 };
 constexpr int kNumVersions = sizeof(kVersions) / sizeof(kVersions[0]);
 constexpr int kAutoVersion = -1; // per-shape choice, the default entry point's policy
@@ -281,12 +281,8 @@ int make_plan(int version, int M, int N, int K, uintptr_t A, uintptr_t B, uintpt
     p.dyn = v.dyn ? 1 : 0;
     p.promote_kb = v.promote ? promote_chunk_kb(v.cta_group == 2 && v.bn == 512 ? 2 : 1, p.num_kb, p.Kp)
                              : p.num_kb;
-    if (v.a_resident) {
-        if (p.num_kb <= kAresMaxKb)
-            p.a_resident = 1;
-        else
-            p.stages = 6; // v2's pipeline
-    }
+    if (v.a_resident && p.num_kb <= kAresMaxKb)
+        p.a_resident = 1; // otherwise v2's plan
     if (v.split_k) {
         // Enough K splits to give every slot (pair or SM) a unit (one wave), at least 8
         // k-blocks per split, and from K = kPromoteMinK on chains of at most kPromoteKb k-blocks.
@@ -690,8 +686,8 @@ cudaError_t dispatch_epi(int epi, int dev, int &max_clusters, bool query_only,
 cudaError_t dispatch(const Plan &p, int dev, int &max_clusters, bool query_only,
                      const CUtensorMap *ma, const CUtensorMap *mb, const CUtensorMap *mc,
                      const GemmArgs *args, int grid, cudaStream_t s) {
-    if (p.a_resident) // v12 with K <= 512
-        return dispatch_epi<2, 256, 4, false, false, false, true>(p.epi, dev, max_clusters, query_only, ma, mb,
+    if (p.a_resident) // v12 with K <= 256
+        return dispatch_epi<2, 256, 6, false, false, false, true>(p.epi, dev, max_clusters, query_only, ma, mb,
                                                                   mc, args, grid, s);
     if (p.cta_group == 1 && p.bn == 256 && p.stages == 4)
         return dispatch_epi<1, 256, 4>(p.epi, dev, max_clusters, query_only, ma, mb, mc, args, grid, s);
