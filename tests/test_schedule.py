@@ -66,7 +66,8 @@ def test_stream_k_plan(vg):
 @pytest.mark.parametrize("shape", [(512, 512, 512), (8192, 8192, 8192), (8191, 8193, 4099), (256, 2048, 1024),
                                    (1000, 3000, 2048), (4096, 14336, 4096), (4096, 4096, 14336),
                                    (8192, 8192, 512), (32768, 32768, 32768), (4096, 32768, 32768),
-                                   (256, 2048, 32768), (1000, 3000, 8192)])
+                                   (256, 2048, 32768), (1000, 3000, 8192), (8192, 8192, 256),
+                                   (1000, 3000, 200)])
 @pytest.mark.parametrize("version", [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12])
 def test_launch_plans_cover_every_iteration_once(vg, shape, version):
     """For the plan the launcher builds (grid, raster group, stream-K or not), the workers'
